@@ -1,0 +1,391 @@
+"""Benchmark of the attention prologue (forward + backward) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload ("C2"): packed forward + backward of
+qknorm_rope_scale on q/k that are strided views of one BF16 QKV buffer
+[T=1,048,576, 3, H=16, D=64], sin/cos FP32 [T, 32] (theta 10000, positions
+restart every 4096 tokens), scales ~N(0, 0.1), upstream gradients ~N(0, 1).
+One step = forward + backward over the T tokens of a rank (weak scaling: every
+rank owns its own T-token shard) followed, at N > 1, by the data-parallel
+reduction of d rmsnorm_weight / d scales over NCCL.
+
+Metric: algorithmic HBM bytes per second of forward + backward (GB/s), plus
+Mtokens/s and the fraction of 8 TB/s. Algorithmic bytes per token:
+forward  H*D*2*4 + D*4 = 8,448 B (read q, k; write q_out, k_out; sin+cos row)
+backward H*D*2*6 + D*4 = 12,544 B (read q, k, dq_out, dk_out; write dq, dk; sin+cos).
+Inputs (6.4 GB buffer) exceed the 126 MB L2, so no flush is needed between steps.
+
+``value`` is timed with CUDA events on the launching stream with inputs resident
+in HBM; ``e2e`` adds, every step, the pinned host->device copy of the step's
+inputs and the device->host copy of its outputs, through the same public API.
+``--impl reference`` times the reference formulation (the CPU oracle port of
+the reference ``native`` backend) on the host cores on a bounded token sample.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "prologue fwd+bwd HBM GB/s (% of 8 TB/s) and Mtokens/s at 1/2/4/8 B200"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+T_TOKENS, HEADS, HEAD_DIM = 1 << 20, 16, 64
+THETA, RESET = 10000.0, 4096
+FWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 4 + HEAD_DIM * 4
+BWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 6 + HEAD_DIM * 4
+# DRAM traffic per launch from one ncu capture (dram__bytes_read.sum +
+# dram__bytes_write.sum) at a reduced T, scaled by tokens; None until captured.
+NCU_TRAFFIC_BYTES_PER_TOKEN = {"fwd": None, "bwd": None}
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def rope_tables(positions, d, theta):
+    inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float64, device=positions.device) / d))
+    ang = (positions.double()[:, None] * inv[None]).float()
+    return ang.sin(), ang.cos()
+
+
+def make_inputs(T, device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    buf = torch.randn(T, 3, HEADS, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+    pos = torch.arange(T, device=device) % RESET
+    sin, cos = rope_tables(pos, HEAD_DIM, THETA)
+    w = 1 + 0.02 * torch.randn(2, 1, HEAD_DIM, generator=g, device=device)
+    s = 0.1 * torch.randn(HEADS, 1, 1, generator=g, device=device)
+    gq = torch.randn(T, HEADS, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+    gk = torch.randn(T, HEADS, HEAD_DIM, generator=g, device=device).to(torch.bfloat16)
+    return buf, w, s, sin, cos, gq, gk
+
+
+def dist_setup(args):
+    """One process per GPU (torchrun env); NCCL process group for our arm at N > 1."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local if world > 1 else 0)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_sample_run(tokens, reps, threads):
+    """Times the reference formulation (oracle port of ``native``) on host cores."""
+    from oracle import native_forward
+    torch.set_num_threads(threads)
+    buf, w, s, sin, cos, gq, gk = make_inputs(tokens, "cpu", 7)
+    q, k = buf[:, 0], buf[:, 1]
+    times = []
+    for i in range(reps + 1):
+        args = [t.detach().requires_grad_(j < 4) for j, t in enumerate((q, k, w, s, sin, cos))]
+        t0 = time.perf_counter()
+        out = native_forward(*args)
+        torch.autograd.grad(out, args[:4], (gq, gk))
+        dt = time.perf_counter() - t0
+        if i > 0:  # first call warms up
+            times.append(dt)
+    per_call = statistics.median(times)
+    gbs = tokens * (FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN) / per_call / 1e9
+    return gbs, per_call
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    tokens = args.cpu_tokens
+    times = []
+    for _ in range(args.warmup):
+        cpu_sample_run(tokens, 1, threads)
+    for _ in range(args.steps):
+        _, per = cpu_sample_run(tokens, 1, threads)
+        times.append(per)
+    per = statistics.median(times)
+    gbs = tokens * (FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN) / per / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "mtokens_per_s": round(tokens / per / 1e6, 4),
+        "config": {"workload": f"C2 packed fwd+bwd, {tokens}-token sample of T=1,048,576, "
+                               f"H={HEADS}, D={HEAD_DIM}, strided views of a [T,3,H,D] BF16 buffer",
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{tokens} tokens of C2 per step (fwd+bwd), torch eager CPU"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    from flash_attn_prologue_b200 import prepare_backend, qknorm_rope_scale
+    from flash_attn_prologue_b200.distributed import reduce_param_grads
+    prepare_backend("cute")
+    device = torch.device("cuda", torch.cuda.current_device())
+    T = args.tokens
+    buf, w, s, sin, cos, gq, gk = make_inputs(T, device, 1234 + rank)
+    q, k = buf[:, 0], buf[:, 1]
+    w.requires_grad_()
+    s.requires_grad_()
+
+    stream = torch.cuda.current_stream()
+    fwd_ev, bwd_ev = [], []
+
+    def step(record=False):
+        qq = q.detach().requires_grad_()
+        kk = k.detach().requires_grad_()
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True); e0.record(stream)
+        out = qknorm_rope_scale(qq, kk, w, s, sin, cos, backend="cute")
+        if record:
+            e1 = torch.cuda.Event(enable_timing=True); e1.record(stream)
+        dq, dk, dw, ds = torch.autograd.grad(out, (qq, kk, w, s), (gq, gk))
+        if record:
+            e2 = torch.cuda.Event(enable_timing=True); e2.record(stream)
+            fwd_ev.append((e0, e1))
+            bwd_ev.append((e1, e2))
+        if world > 1:
+            dw, ds = reduce_param_grads(dw, ds)
+        return out, dq, dk, dw, ds
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            step(record=True)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
+    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_ev)
+    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in bwd_ev)
+
+    ms_per_step = elapsed_ms / args.steps
+    step_bytes = T * (FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN)
+    value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
+    mtok = world * T / (ms_per_step * 1e-3) / 1e6
+
+    # ---- end to end: host buffers through the public API, copies timed ----
+    e2e = run_e2e(args, T, device, w, s, world)
+
+    peak, peak_kind = measured_peak()
+    bwd_bytes = T * BWD_BYTES_PER_TOKEN
+    fwd_bytes = T * FWD_BYTES_PER_TOKEN
+    bwd_gbs = bwd_bytes / (bwd_ms * 1e-3) / 1e9
+    fwd_gbs = fwd_bytes / (fwd_ms * 1e-3) / 1e9
+    traffic = NCU_TRAFFIC_BYTES_PER_TOKEN["bwd"]
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"C2 packed fwd+bwd, T={T} tokens per GPU, H={HEADS}, D={HEAD_DIM}, "
+                               "q/k strided views of a [T,3,H,D] BF16 QKV buffer, sin/cos FP32 [T,32]",
+                   "tokens_per_gpu": T, "heads": HEADS, "head_dim": HEAD_DIM,
+                   "l2": "inputs larger than L2 (6.4 GB buffer per GPU), no flush",
+                   "parallelism": f"dp{world}"},
+        "mtokens_per_s": round(mtok, 3),
+        "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 2),
+        "fwd": {"ms": round(fwd_ms, 4), "gbs": round(fwd_gbs, 1),
+                "frac_of_measured": round(fwd_gbs / peak, 4),
+                "pct_of_8tbs": round(100 * fwd_gbs / NOMINAL_HBM_GBS, 2)},
+        "bwd": {"ms": round(bwd_ms, 4), "gbs": round(bwd_gbs, 1),
+                "frac_of_measured": round(bwd_gbs / peak, 4),
+                "pct_of_8tbs": round(100 * bwd_gbs / NOMINAL_HBM_GBS, 2)},
+        "roofline": {"kernel": "prologue_bwd_kernel (+ finalize)", "bound": "hbm",
+                     "achieved": round(bwd_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(bwd_gbs / peak, 4), "peak_source": peak_kind,
+                     "traffic": (round(traffic * T) if traffic else None)},
+        "e2e": e2e,
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        gbs, per = cpu_sample_run(args.cpu_tokens, args.cpu_reps, threads)
+        line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
+                                "kind": "port",
+                                "sample": f"{args.cpu_tokens} tokens of C2 fwd+bwd, median of "
+                                          f"{args.cpu_reps}, torch eager CPU port of native"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, T, device, w, s, world):
+    """Same metric with pinned host buffers: H2D inputs + D2H outputs inside the timing."""
+    from flash_attn_prologue_b200 import qknorm_rope_scale
+    g = torch.Generator().manual_seed(99)
+    tok = min(T, args.e2e_tokens)
+    h_q = torch.randn(tok, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).pin_memory()
+    h_k = torch.randn(tok, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).pin_memory()
+    h_gq = torch.randn(tok, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).pin_memory()
+    h_gk = torch.randn(tok, HEADS, HEAD_DIM, generator=g).to(torch.bfloat16).pin_memory()
+    sin, cos = rope_tables(torch.arange(tok) % RESET, HEAD_DIM, THETA)
+    h_sin, h_cos = sin.pin_memory(), cos.pin_memory()
+    outs = [torch.empty(tok, HEADS, HEAD_DIM, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    h_dw = torch.empty(2, 1, HEAD_DIM).pin_memory()
+    h_ds = torch.empty(HEADS, 1, 1).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_gq, h_gk, h_sin, h_cos))
+    d2h = sum(t.numel() * t.element_size() for t in outs) + (h_dw.numel() + h_ds.numel()) * 4
+    stream = torch.cuda.current_stream()
+
+    def step():
+        q = h_q.to(device, non_blocking=True).requires_grad_()
+        k = h_k.to(device, non_blocking=True).requires_grad_()
+        gq = h_gq.to(device, non_blocking=True)
+        gk = h_gk.to(device, non_blocking=True)
+        sn = h_sin.to(device, non_blocking=True)
+        cs = h_cos.to(device, non_blocking=True)
+        out = qknorm_rope_scale(q, k, w, s, sn, cs, backend="cute")
+        dq, dk, dw, ds = torch.autograd.grad(out, (q, k, w, s), (gq, gk))
+        for dst, src in zip(outs, (out[0], out[1], dq, dk)):
+            dst.copy_(src, non_blocking=True)
+        h_dw.copy_(dw, non_blocking=True)
+        h_ds.copy_(ds, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    steps = max(1, min(args.steps, 10))
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), world) / steps
+    gbs = world * tok * (FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN) / (ms * 1e-3) / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3), "tokens_per_step": tok,
+            "path": "qknorm_rope_scale(backend='cute') -> torch.library op -> C ABI"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=T_TOKENS, help="tokens per GPU (default: C2)")
+    ap.add_argument("--e2e-tokens", type=int, default=T_TOKENS // 4)
+    ap.add_argument("--cpu-tokens", type=int, default=32768)
+    ap.add_argument("--cpu-reps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        # The reference path is CPU code: rank 0 runs it, other ranks exit at once.
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args)
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

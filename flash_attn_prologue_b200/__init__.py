@@ -1,0 +1,30 @@
+"""B200-native (sm_100a) attention prologue: Q/K RMSNorm -> split-half RoPE -> Q scale.
+
+Public API (same names as flash_attn_prologue/__init__.py:1-19):
+``qknorm_rope_scale``, ``prepare_backend``, ``RMSNormRoPEScale``. The custom-op
+callables are exported lazily under the reference's names, so importing the
+package touches neither CUDA nor the shared library, and changes no
+environment variable.
+"""
+from importlib import import_module
+
+from .functional import prepare_backend, qknorm_rope_scale
+from .layers.RMSNorm import RMSNormRoPEScale
+
+__version__ = "0.2.0"
+
+_LAZY = {
+    "qknorm_rope_scale_cute_op": ("fused_epilogue", "qknorm_rope_scale_cute_op"),
+    "qknorm_rope_scale_cute_backward_op": ("fused_epilogue", "qknorm_rope_scale_cute_backward_op"),
+}
+__all__ = ["qknorm_rope_scale", "prepare_backend", "RMSNormRoPEScale", *_LAZY]
+
+
+def __getattr__(name):
+    if name not in _LAZY:
+        raise AttributeError(name)
+    module, symbol = _LAZY[name]
+    loaded = import_module(f".{module}", __name__)
+    value = getattr(loaded, symbol)
+    globals()[name] = value
+    return value

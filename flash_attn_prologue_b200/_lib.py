@@ -1,0 +1,104 @@
+"""ctypes binding of libflash_prologue.so (declarations: include/flash_prologue.h).
+
+The library is built in-tree by ``python -m flash_attn_prologue_b200.build``
+(or ``__graft_entry__.build()``). Loading is lazy: importing the package never
+touches CUDA or the library. There is no fallback: a missing library raises.
+"""
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(__file__).resolve().parent / "libflash_prologue.so"
+_lock = threading.Lock()
+_lib = None
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_UNSUPPORTED = 2
+ERR_CHANNEL_STRIDE = 3
+ERR_EXPANDED = 4
+ERR_WORKSPACE = 5
+ERR_CUDA = 6
+ERR_ALIGNMENT = 7
+
+DTYPE_CODES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+_i64p = ctypes.POINTER(ctypes.c_int64)
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+
+SIGNATURES = {
+    "flash_prologue_status_string": ([ctypes.c_int], ctypes.c_char_p),
+    "flash_prologue_version": ([], ctypes.c_int),
+    "flash_prologue_fwd": ([_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
+                            _vp, _i64p, _vp, _i64p, _i64, _i64, _i64, _i64,
+                            ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
+    "flash_prologue_bwd_workspace_size": ([_i64, _i64, _i64, _i64, ctypes.c_int,
+                                           ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "flash_prologue_bwd": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,
+                            _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
+                            _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64,
+                            ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
+}
+
+
+class PrologueError(RuntimeError):
+    """A CUDA-side failure reported by libflash_prologue.so."""
+
+
+def lib_path() -> Path:
+    return _LIB_PATH
+
+
+def load():
+    """Loads (once) and returns the ctypes handle; raises if the library is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not _LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{_LIB_PATH.name} is not built; run `python -m flash_attn_prologue_b200.build` "
+                    "(the CUDA kernels have no CPU fallback)")
+            handle = ctypes.CDLL(os.fspath(_LIB_PATH))
+            for name, (argtypes, restype) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.argtypes = argtypes
+                fn.restype = restype
+            _lib = handle
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return load().flash_prologue_status_string(status).decode()
+
+
+def check(status: int, what: str) -> None:
+    """Maps a library status to the exception the reference raises for it."""
+    if status == OK:
+        return
+    msg = f"{what}: {status_string(status)}"
+    if status in (ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CHANNEL_STRIDE, ERR_EXPANDED,
+                  ERR_ALIGNMENT, ERR_WORKSPACE):
+        raise ValueError(msg)
+    raise PrologueError(msg)
+
+
+def strides4(t: torch.Tensor):
+    return (ctypes.c_int64 * 4)(*t.stride())
+
+
+def strides3(values):
+    return (ctypes.c_int64 * 3)(*values)
+
+
+def ptr(t: torch.Tensor):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)

@@ -1,0 +1,299 @@
+// C ABI of libflash_prologue.so: argument validation, layout planning and
+// dispatch to the kernel launchers. Declarations: include/flash_prologue.h.
+#include <math.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "../../include/flash_prologue.h"
+#include "prologue_host.h"
+
+namespace flash_prologue {
+
+namespace {
+
+int log2_exact(int64_t v) {
+  int r = 0;
+  while ((int64_t(1) << r) < v) ++r;
+  return r;
+}
+
+int64_t pow2_floor(int64_t v) {
+  int64_t p = 1;
+  while (p * 2 <= v) p *= 2;
+  return p;
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+Geometry plan_geometry(int64_t B, int64_t H, int64_t N, int D, bool heads_inner) {
+  Geometry g{};
+  const int L = D / 16;
+  const int slots = kThreads / L;
+  const int warp_slots = 32 / L;
+  g.log2_l = log2_exact(L);
+  g.heads_inner = heads_inner ? 1 : 0;
+  int64_t hs, ps;
+  if (heads_inner) {
+    // Head slots along lanes: the largest power of two dividing H (no idle
+    // lanes), unless that leaves a warp mostly spread over positions.
+    hs = 1;
+    while (hs * 2 <= slots && H % (hs * 2) == 0) hs *= 2;
+    if (hs < 4 && hs < H) hs = pow2_floor(H < slots ? H : slots);
+    ps = slots / hs;
+    g.hi = (int)cdiv(H, hs);
+  } else {
+    ps = warp_slots >= 8 ? warp_slots : 8;
+    if (ps > slots) ps = slots;
+    hs = slots / ps;
+    int64_t hi = cdiv(H, hs);
+    g.hi = (int)(hi < 8 ? hi : 8);
+  }
+  g.log2_hs = log2_exact(hs);
+  g.log2_ps = log2_exact(ps);
+  g.n_pos_blocks = cdiv(N, ps);
+  g.n_head_groups = cdiv(H, (int64_t)g.hi * hs);
+  g.n_items = 2 * B * g.n_pos_blocks * g.n_head_groups;
+  return g;
+}
+
+int64_t persistent_grid(const void* kernel, size_t smem_bytes, int64_t n_items) {
+  struct Key {
+    const void* fn;
+    size_t smem;
+    int dev;
+    bool operator==(const Key& o) const { return fn == o.fn && smem == o.smem && dev == o.dev; }
+  };
+  struct KeyHash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.fn) ^ (k.smem * 1315423911u) ^ ((size_t)k.dev << 48);
+    }
+  };
+  static std::mutex mu;
+  static std::unordered_map<Key, int64_t, KeyHash> cache;  // resident CTAs per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  Key key{kernel, smem_bytes, dev};
+  int64_t resident = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) resident = it->second;
+  }
+  if (resident == 0) {
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem_bytes) !=
+        cudaSuccess)
+      return -1;
+    if (per_sm < 1) per_sm = 1;
+    resident = (int64_t)sms * per_sm;
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = resident;
+  }
+  return n_items < resident ? n_items : resident;
+}
+
+}  // namespace flash_prologue
+
+using namespace flash_prologue;
+
+namespace {
+
+constexpr int64_t kMaxHeads = 512;
+
+bool supported_dim(int64_t D) { return D == 32 || D == 64 || D == 128 || D == 256; }
+
+size_t elem_size(int dtype) { return dtype == FLASH_PROLOGUE_FP32 ? 4 : 2; }
+
+// Activation view checks: d stride 1, and no broadcast (stride 0) on a dim of size > 1.
+int check_view(const int64_t s[4], int64_t B, int64_t H, int64_t N) {
+  if (s[3] != 1) return FLASH_PROLOGUE_ERR_CHANNEL_STRIDE;
+  if ((B > 1 && s[0] == 0) || (H > 1 && s[1] == 0) || (N > 1 && s[2] == 0))
+    return FLASH_PROLOGUE_ERR_EXPANDED;
+  return FLASH_PROLOGUE_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 16-byte vector path: base 16-byte aligned and every row start 16-byte aligned.
+bool view_vec_ok(const void* p, const int64_t s[4], size_t es) {
+  if (!aligned16(p)) return false;
+  for (int i = 0; i < 3; ++i)
+    if (((s[i] * (int64_t)es) & 15) != 0) return false;
+  return true;
+}
+
+bool table_vec_ok(const float* p, const int64_t s[3]) {
+  if (!aligned16(p) || s[2] != 1) return false;
+  return ((s[0] * 4) & 15) == 0 && ((s[1] * 4) & 15) == 0;
+}
+
+RowStrides rows(const int64_t s[4]) { return RowStrides{s[0], s[1], s[2]}; }
+TableStrides table(const int64_t s[3]) { return TableStrides{s[0], s[1], s[2]}; }
+
+bool heads_inner_layout(const int64_t s[4], int64_t H, int64_t N) {
+  if (N == 1) return true;
+  if (H == 1) return false;
+  const int64_t sh = s[1] < 0 ? -s[1] : s[1];
+  const int64_t sn = s[2] < 0 ? -s[2] : s[2];
+  return sh <= sn;
+}
+
+int common_checks(const void* q, const int64_t* qs, const void* k, const int64_t* ks,
+                  const float* w, const float* sc, const float* sin, const int64_t* sins,
+                  const float* cos, const int64_t* coss, int64_t B, int64_t H, int64_t N,
+                  int64_t D, float eps, int dtype) {
+  if (B < 0 || H < 0 || N < 0 || D <= 0) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  if (!(eps > 0.f) || !isfinite(eps)) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  if (dtype < 0 || dtype > 2 || !supported_dim(D)) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
+  if (H > kMaxHeads) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
+  if (!qs || !ks || !sins || !coss) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  if (B * H * N == 0) return FLASH_PROLOGUE_OK;
+  if (!q || !k || !w || !sc || !sin || !cos) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  int st = check_view(qs, B, H, N);
+  if (st == FLASH_PROLOGUE_OK) st = check_view(ks, B, H, N);
+  return st;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* flash_prologue_status_string(int status) {
+  switch (status) {
+    case FLASH_PROLOGUE_OK: return "ok";
+    case FLASH_PROLOGUE_ERR_INVALID_ARGUMENT: return "invalid argument (size, null pointer or eps)";
+    case FLASH_PROLOGUE_ERR_UNSUPPORTED: return "unsupported head dimension, head count or dtype";
+    case FLASH_PROLOGUE_ERR_CHANNEL_STRIDE: return "channel stride must be 1";
+    case FLASH_PROLOGUE_ERR_EXPANDED: return "expanded activations (stride 0 on a dimension of size > 1) are not supported";
+    case FLASH_PROLOGUE_ERR_WORKSPACE: return "workspace missing or too small";
+    case FLASH_PROLOGUE_ERR_CUDA: return "CUDA launch or runtime error";
+    case FLASH_PROLOGUE_ERR_ALIGNMENT: return "pointer alignment not supported";
+    default: return "unknown status";
+  }
+}
+
+int flash_prologue_version(void) { return 100; }
+
+int flash_prologue_fwd(const void* q, const int64_t q_strides[4], const void* k,
+                       const int64_t k_strides[4], void* q_out, const int64_t q_out_strides[4],
+                       void* k_out, const int64_t k_out_strides[4], const float* rmsnorm_weight,
+                       const float* scales, const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3], int64_t B, int64_t H,
+                       int64_t N, int64_t D, float eps, int dtype, void* stream) {
+  int st = common_checks(q, q_strides, k, k_strides, rmsnorm_weight, scales, sin, sin_strides, cos,
+                         cos_strides, B, H, N, D, eps, dtype);
+  if (st != FLASH_PROLOGUE_OK || B * H * N == 0) return st;
+  if (!q_out || !k_out || !q_out_strides || !k_out_strides) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  st = check_view(q_out_strides, B, H, N);
+  if (st == FLASH_PROLOGUE_OK) st = check_view(k_out_strides, B, H, N);
+  if (st != FLASH_PROLOGUE_OK) return st;
+
+  const size_t es = elem_size(dtype);
+  const bool vec = view_vec_ok(q, q_strides, es) && view_vec_ok(k, k_strides, es) &&
+                   view_vec_ok(q_out, q_out_strides, es) && view_vec_ok(k_out, k_out_strides, es) &&
+                   table_vec_ok(sin, sin_strides) && table_vec_ok(cos, cos_strides);
+  FwdArgs a{};
+  a.x[0] = q; a.x[1] = k; a.y[0] = q_out; a.y[1] = k_out;
+  a.sx[0] = rows(q_strides); a.sx[1] = rows(k_strides);
+  a.sy[0] = rows(q_out_strides); a.sy[1] = rows(k_out_strides);
+  a.w = rmsnorm_weight; a.scales = scales; a.sin = sin; a.cos = cos;
+  a.ssin = table(sin_strides); a.scos = table(cos_strides);
+  a.B = B; a.N = N; a.H = (int)H; a.eps = eps;
+  a.g = plan_geometry(B, H, N, (int)D, heads_inner_layout(q_strides, H, N));
+  cudaError_t err = launch_fwd(a, dtype, (int)D, vec, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
+}
+
+static int bwd_plan(int64_t B, int64_t H, int64_t N, int64_t D, int dtype, bool vec,
+                    bool heads_inner, Geometry* g, int64_t* grid) {
+  *g = plan_geometry(B, H, N, (int)D, heads_inner);
+  *grid = bwd_grid(*g, (int)H, (int)D, dtype, vec);
+  return *grid > 0 ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
+}
+
+int flash_prologue_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D, int dtype,
+                                      size_t* bytes) {
+  if (!bytes) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  *bytes = 0;
+  if (B < 0 || H < 0 || N < 0) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  if (dtype < 0 || dtype > 2 || !supported_dim(D) || H > kMaxHeads) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
+  if (B * H * N == 0) return FLASH_PROLOGUE_OK;
+  // The grid (and so the workspace) is the largest of the layouts and vector
+  // widths the call may pick, so one size serves every stride pattern.
+  int64_t worst = 0;
+  for (int hi = 0; hi < 2; ++hi) {
+    for (int v = 0; v < 2; ++v) {
+      Geometry g;
+      int64_t grid;
+      int st = bwd_plan(B, H, N, D, dtype, v != 0, hi != 0, &g, &grid);
+      if (st != FLASH_PROLOGUE_OK) return st;
+      if (grid > worst) worst = grid;
+    }
+  }
+  *bytes = (size_t)worst * (size_t)(2 * D + H) * sizeof(float);
+  return FLASH_PROLOGUE_OK;
+}
+
+int flash_prologue_bwd(const void* q, const int64_t q_strides[4], const void* k,
+                       const int64_t k_strides[4], const float* rmsnorm_weight,
+                       const float* scales, const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3], const void* grad_q_out,
+                       const int64_t gq_strides[4], const void* grad_k_out,
+                       const int64_t gk_strides[4], void* grad_q, const int64_t dq_strides[4],
+                       void* grad_k, const int64_t dk_strides[4], float* grad_rmsnorm_weight,
+                       float* grad_scales, void* workspace, size_t workspace_bytes, int64_t B,
+                       int64_t H, int64_t N, int64_t D, float eps, int dtype, void* stream) {
+  int st = common_checks(q, q_strides, k, k_strides, rmsnorm_weight, scales, sin, sin_strides, cos,
+                         cos_strides, B, H, N, D, eps, dtype);
+  if (st != FLASH_PROLOGUE_OK) return st;
+  if (!grad_rmsnorm_weight || !grad_scales) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (B * H * N == 0) {
+    // No rows: the parameter gradients are exactly zero.
+    if (cudaMemsetAsync(grad_rmsnorm_weight, 0, sizeof(float) * 2 * D, s) != cudaSuccess ||
+        (H > 0 && cudaMemsetAsync(grad_scales, 0, sizeof(float) * H, s) != cudaSuccess))
+      return FLASH_PROLOGUE_ERR_CUDA;
+    return FLASH_PROLOGUE_OK;
+  }
+  if (!grad_q_out || !grad_k_out || !grad_q || !grad_k || !gq_strides || !gk_strides ||
+      !dq_strides || !dk_strides)
+    return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  // Upstream gradients are only read, so broadcast (stride-0) views such as the
+  // gradient of a sum() are read in place; their d stride must still be 1.
+  if (gq_strides[3] != 1 || gk_strides[3] != 1) return FLASH_PROLOGUE_ERR_CHANNEL_STRIDE;
+  st = check_view(dq_strides, B, H, N);
+  if (st == FLASH_PROLOGUE_OK) st = check_view(dk_strides, B, H, N);
+  if (st != FLASH_PROLOGUE_OK) return st;
+
+  const size_t es = elem_size(dtype);
+  const bool vec = view_vec_ok(q, q_strides, es) && view_vec_ok(k, k_strides, es) &&
+                   view_vec_ok(grad_q_out, gq_strides, es) && view_vec_ok(grad_k_out, gk_strides, es) &&
+                   view_vec_ok(grad_q, dq_strides, es) && view_vec_ok(grad_k, dk_strides, es) &&
+                   table_vec_ok(sin, sin_strides) && table_vec_ok(cos, cos_strides);
+  Geometry g;
+  int64_t grid;
+  st = bwd_plan(B, H, N, D, dtype, vec, heads_inner_layout(q_strides, H, N), &g, &grid);
+  if (st != FLASH_PROLOGUE_OK) return st;
+  const size_t need = (size_t)grid * (size_t)(2 * D + H) * sizeof(float);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace)) return FLASH_PROLOGUE_ERR_WORKSPACE;
+
+  BwdArgs a{};
+  a.x[0] = q; a.x[1] = k; a.gy[0] = grad_q_out; a.gy[1] = grad_k_out;
+  a.dx[0] = grad_q; a.dx[1] = grad_k;
+  a.sx[0] = rows(q_strides); a.sx[1] = rows(k_strides);
+  a.sgy[0] = rows(gq_strides); a.sgy[1] = rows(gk_strides);
+  a.sdx[0] = rows(dq_strides); a.sdx[1] = rows(dk_strides);
+  a.w = rmsnorm_weight; a.scales = scales; a.sin = sin; a.cos = cos;
+  a.ssin = table(sin_strides); a.scos = table(cos_strides);
+  a.partials = static_cast<float*>(workspace);
+  a.B = B; a.N = N; a.H = (int)H; a.eps = eps;
+  a.g = g;
+  cudaError_t err = launch_bwd(a, grad_rmsnorm_weight, grad_scales, dtype, (int)D, vec, s);
+  return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,280 @@
+// Backward prologue: dq, dk and the weight / log-scale gradients in one pass
+// over q, k, grad_q_out, grad_k_out, followed by a small fixed-order reduction.
+//
+// Per row (x = q or k, g = upstream gradient, e = exp(scales[h]) for Q, 1 for K),
+// the identities of the reference backward (flash_attn_prologue/fused_epilogue.py:1047-1126):
+//   r  = 1/sqrt(mean(x^2)+eps),  n = x*r
+//   g' = g*e
+//   dn_j = g'_j cos_j + g'_{j+D/2} sin_j,  dn_{j+D/2} = g'_{j+D/2} cos_j - g'_j sin_j
+//   d scales[h]   += sum_j g'_j * rot(n*w)_j           (Q rows only)
+//   d w[t][j]     += dn_j * n_j
+//   dx_j = r * (dn_j w_j - n_j * sum_i(dn_i w_i n_i) / D)
+// The reference accumulates the two parameter gradients with float atomics
+// (fused_epilogue.py:1129-1207), whose order changes run to run. Here every
+// CTA owns fixed rows (persistent, round-robin items); its threads keep
+// register/shared partials that are combined in a fixed order into one
+// [2*D + H] partial per CTA, and a second kernel sums the CTA partials in CTA
+// order. The result is bit-identical on every run with the same grid.
+#include "prologue_host.h"
+
+namespace flash_prologue {
+
+template <typename T, int D, bool VEC>
+__global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a) {
+  constexpr int L = D / 16;
+  constexpr int HALF = D / 2;
+  constexpr int LOG2_L = (L == 2) ? 1 : (L == 4) ? 2 : (L == 8) ? 3 : 4;
+  extern __shared__ float smem[];
+  float* w_s = smem;                       // [2 * D]
+  float* e_s = w_s + 2 * D;                // [H]
+  float* ds_s = e_s + a.H;                 // [kWarps][H]
+  float* dw_s = ds_s + kWarps * a.H;       // [kWarps][D]
+  for (int i = threadIdx.x; i < 2 * D; i += kThreads) w_s[i] = a.w[i];
+  for (int i = threadIdx.x; i < a.H; i += kThreads) e_s[i] = (float)exp((double)a.scales[i]);
+  for (int i = threadIdx.x; i < kWarps * a.H; i += kThreads) ds_s[i] = 0.f;
+  __syncthreads();
+
+  // The host makes the grid even (or equal to the even item count), so every
+  // item of this CTA has the tensor index of its first item.
+  const int t = blockIdx.x & 1;
+  const T* xb = static_cast<const T*>(a.x[t]);
+  const T* gb = static_cast<const T*>(a.gy[t]);
+  T* db = static_cast<T*>(a.dx[t]);
+  const RowStrides sx = a.sx[t], sg = a.sgy[t], sd = a.sdx[t];
+  const float* w = w_s + t * D;
+
+  int c, hs, ps;
+  thread_slots(a.g, threadIdx.x, c, hs, ps);
+  const int HS = 1 << a.g.log2_hs;
+  const int PS = 1 << a.g.log2_ps;
+  const int heads_per_item = a.g.hi * HS;
+  const int j0 = c * kChunk;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+
+  // Lane bits (within the warp) that select a position slot: lanes that differ
+  // only in these bits and in the chunk bits hold rows of the same head.
+  const int warp_slot_bits = 5 - LOG2_L;
+  int ps_lo, ps_hi;  // ps bits occupy lane bits [ps_lo, ps_hi)
+  if (a.g.heads_inner) {
+    ps_lo = LOG2_L + min(a.g.log2_hs, warp_slot_bits);
+    ps_hi = 5;
+  } else {
+    ps_lo = LOG2_L;
+    ps_hi = LOG2_L + min(a.g.log2_ps, warp_slot_bits);
+  }
+  const bool ds_writer = (lane & ((1 << ps_hi) - 1) & ~((1 << ps_lo) - 1)) == 0 && c == 0;
+
+  float acc1[kChunk], acc2[kChunk];  // d w partials for elements j0.. and HALF+j0..
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) { acc1[j] = 0.f; acc2[j] = 0.f; }
+
+  for (int64_t item = blockIdx.x; item < a.g.n_items; item += gridDim.x) {
+    int ti;
+    int64_t b, pb, hg;
+    item_coords(a.g, item, ti, b, pb, hg);
+    const int64_t n = pb * PS + ps;
+    const bool pos_ok = n < a.N;
+
+    float sn[kChunk], cs[kChunk];
+    if (pos_ok) {
+      load_table<VEC>(sn, a.sin + b * a.ssin.b + n * a.ssin.n + (int64_t)j0 * a.ssin.j, a.ssin.j);
+      load_table<VEC>(cs, a.cos + b * a.scos.b + n * a.scos.n + (int64_t)j0 * a.scos.j, a.scos.j);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) { sn[j] = 0.f; cs[j] = 0.f; }
+    }
+
+    for (int i = 0; i < a.g.hi; ++i) {
+      const int h = (int)hg * heads_per_item + i * HS + hs;
+      const bool ok = pos_ok && h < a.H;
+      Chunk<T> x1, x2, g1, g2;
+      if (ok) {
+        const T* xp = xb + b * sx.b + (int64_t)h * sx.h + n * sx.n + j0;
+        const T* gp = gb + b * sg.b + (int64_t)h * sg.h + n * sg.n + j0;
+        load_stream<T, VEC>(x1, xp);
+        load_stream<T, VEC>(x2, xp + HALF);
+        load_stream<T, VEC>(g1, gp);
+        load_stream<T, VEC>(g2, gp + HALF);
+      } else {
+#pragma unroll
+        for (int k = 0; k < Chunk<T>::kWords; ++k) { x1.w[k] = 0; x2.w[k] = 0; g1.w[k] = 0; g2.w[k] = 0; }
+      }
+      const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
+
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        float v = chunk_get(x1, j); ss = __fadd_rn(ss, __fmul_rn(v, v));
+      }
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        float v = chunk_get(x2, j); ss = __fadd_rn(ss, __fmul_rn(v, v));
+      }
+      ss = row_sum<L>(ss);
+      const float r = inv_rms<D>(ss, a.eps);
+
+      float dsum = 0.f, ds_part = 0.f;
+      float dn1[kChunk], dn2[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const float n1 = chunk_get(x1, j) * r, n2 = chunk_get(x2, j) * r;
+        const float gg1 = chunk_get(g1, j) * e, gg2 = chunk_get(g2, j) * e;
+        const float d1 = gg1 * cs[j] + gg2 * sn[j];
+        const float d2 = gg2 * cs[j] - gg1 * sn[j];
+        const float wa = w[j0 + j], wb = w[HALF + j0 + j];
+        if (t == 0) {
+          const float ya = n1 * wa, yb = n2 * wb;
+          ds_part += gg1 * (ya * cs[j] - yb * sn[j]) + gg2 * (yb * cs[j] + ya * sn[j]);
+        }
+        acc1[j] += d1 * n1;
+        acc2[j] += d2 * n2;
+        dsum += d1 * wa * n1 + d2 * wb * n2;
+        dn1[j] = d1;
+        dn2[j] = d2;
+      }
+      dsum = row_sum<L>(dsum);
+      if (t == 0) {
+        // d scales: reduce over the row's lanes and the warp's position slots.
+        ds_part = row_sum<L>(ds_part);
+        for (int bit = ps_lo; bit < ps_hi; ++bit)
+          ds_part = __fadd_rn(ds_part, __shfl_xor_sync(0xffffffffu, ds_part, 1 << bit));
+        if (ds_writer && h < a.H) ds_s[warp * a.H + h] += ds_part;
+      }
+
+      if (!ok) continue;
+      const float m = dsum * (1.0f / (float)D);
+      float o1[kChunk], o2[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const float n1 = chunk_get(x1, j) * r, n2 = chunk_get(x2, j) * r;
+        o1[j] = r * (dn1[j] * w[j0 + j] - n1 * m);
+        o2[j] = r * (dn2[j] * w[HALF + j0 + j] - n2 * m);
+      }
+      Chunk<T> out;
+      T* dp = db + b * sd.b + (int64_t)h * sd.h + n * sd.n + j0;
+      chunk_set(out, o1);
+      store_stream<T, VEC>(dp, out);
+      chunk_set(out, o2);
+      store_stream<T, VEC>(dp + HALF, out);
+    }
+  }
+
+  // d w: combine lanes that hold the same chunk (fixed xor order), then warps.
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) {
+#pragma unroll
+    for (int o = L; o < 32; o <<= 1) {
+      acc1[j] = __fadd_rn(acc1[j], __shfl_xor_sync(0xffffffffu, acc1[j], o));
+      acc2[j] = __fadd_rn(acc2[j], __shfl_xor_sync(0xffffffffu, acc2[j], o));
+    }
+  }
+  if (lane < L) {
+    float* dst = dw_s + warp * D;
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      dst[j0 + j] = acc1[j];
+      dst[HALF + j0 + j] = acc2[j];
+    }
+  }
+  __syncthreads();
+  const int C = 2 * D + a.H;
+  float* out = a.partials + (int64_t)blockIdx.x * C;
+  for (int col = threadIdx.x; col < C; col += kThreads) {
+    float v = 0.f;
+    if (col < 2 * D) {
+      if ((col >= D) == (t == 1)) {
+        const int j = col - t * D;
+#pragma unroll
+        for (int w8 = 0; w8 < kWarps; ++w8) v = __fadd_rn(v, dw_s[w8 * D + j]);
+      }
+    } else if (t == 0) {
+#pragma unroll
+      for (int w8 = 0; w8 < kWarps; ++w8) v = __fadd_rn(v, ds_s[w8 * a.H + (col - 2 * D)]);
+    }
+    out[col] = v;
+  }
+}
+
+// Sums the [G, C] CTA partials over G in a fixed order: warp w of CTA x sums
+// rows w, w+8, ... of 32 columns; the 8 warp sums are then added in warp order.
+__global__ void __launch_bounds__(kThreads) prologue_bwd_finalize_kernel(
+    const float* __restrict__ partials, int64_t G, int C, int two_d, float* __restrict__ dw,
+    float* __restrict__ ds) {
+  __shared__ float part[kWarps][32];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float v = 0.f;
+  if (col < C)
+    for (int64_t g = warp; g < G; g += kWarps) v = __fadd_rn(v, partials[g * C + col]);
+  part[warp][lane] = v;
+  __syncthreads();
+  if (warp == 0 && col < C) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, part[w][lane]);
+    if (col < two_d) dw[col] = s;
+    else ds[col - two_d] = s;
+  }
+}
+
+size_t bwd_smem_bytes(int H, int D) {
+  return (size_t)(2 * D + H + kWarps * H + kWarps * D) * sizeof(float);
+}
+
+// Grid for the backward kernel: persistent, and even whenever it is smaller
+// than the (always even) item count, so each CTA sees a single tensor.
+static int64_t even_grid(int64_t grid, int64_t n_items) {
+  if (grid >= n_items) return n_items;
+  return grid >= 2 ? (grid & ~int64_t(1)) : 2;
+}
+
+template <typename T, int D, bool VEC>
+static const void* bwd_kernel_ptr() {
+  return reinterpret_cast<const void*>(&prologue_bwd_kernel<T, D, VEC>);
+}
+
+static const void* bwd_kernel_for(int dtype, int D, bool vec) {
+#define FP_BWD_CASE(T)                                                              \
+  switch (D) {                                                                      \
+    case 32: return vec ? bwd_kernel_ptr<T, 32, true>() : bwd_kernel_ptr<T, 32, false>();   \
+    case 64: return vec ? bwd_kernel_ptr<T, 64, true>() : bwd_kernel_ptr<T, 64, false>();   \
+    case 128: return vec ? bwd_kernel_ptr<T, 128, true>() : bwd_kernel_ptr<T, 128, false>(); \
+    case 256: return vec ? bwd_kernel_ptr<T, 256, true>() : bwd_kernel_ptr<T, 256, false>(); \
+    default: return nullptr;                                                        \
+  }
+  switch (dtype) {
+    case 0: FP_BWD_CASE(__nv_bfloat16)
+    case 1: FP_BWD_CASE(__half)
+    case 2: FP_BWD_CASE(float)
+    default: return nullptr;
+  }
+#undef FP_BWD_CASE
+}
+
+int64_t bwd_grid(const Geometry& g, int H, int D, int dtype, bool vec) {
+  const void* fn = bwd_kernel_for(dtype, D, vec);
+  if (!fn) return -1;
+  const int64_t grid = persistent_grid(fn, bwd_smem_bytes(H, D), g.n_items);
+  return grid > 0 ? even_grid(grid, g.n_items) : grid;
+}
+
+cudaError_t launch_bwd(const BwdArgs& a, float* dw, float* ds, int dtype, int D, bool vec,
+                       cudaStream_t stream) {
+  const void* fn = bwd_kernel_for(dtype, D, vec);
+  if (!fn) return cudaErrorInvalidValue;
+  const size_t smem = bwd_smem_bytes(a.H, D);
+  int64_t grid = persistent_grid(fn, smem, a.g.n_items);
+  if (grid <= 0) return cudaErrorInvalidConfiguration;
+  grid = even_grid(grid, a.g.n_items);
+  void* args[] = {const_cast<BwdArgs*>(&a)};
+  cudaError_t err = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kThreads), args, smem, stream);
+  if (err != cudaSuccess) return err;
+  const int C = 2 * D + a.H;
+  prologue_bwd_finalize_kernel<<<(C + 31) / 32, kThreads, 0, stream>>>(a.partials, grid, C, 2 * D,
+                                                                        dw, ds);
+  return cudaGetLastError();
+}
+
+}  // namespace flash_prologue

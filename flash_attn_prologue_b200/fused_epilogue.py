@@ -1,0 +1,266 @@
+"""``torch.library`` custom ops of the prologue, backed by libflash_prologue.so.
+
+Registers, under the reference's names and schemas:
+
+* ``flash_prologue::qknorm_rope_scale_cute`` (reference:
+  flash_attn_prologue/fused_epilogue.py:702-815, fake :817-828);
+* ``flash_prologue::qknorm_rope_scale_cute_backward`` (reference:
+  fused_epilogue.py:1304-1423, fake :1425-1437);
+* the autograd link between them (reference: fused_epilogue.py:1440-1458).
+
+Raw-op contract kept from the reference: q/k are 4-D ``[B, H, N, D]`` views
+with channel stride 1 and no expanded (stride-0) dimension, rejected with the
+same ValueError texts ("expanded activations", "channel stride"); outputs and
+input gradients use the compact-by-permutation strides of the inputs; sin/cos
+are FP32, broadcastable to ``[B, 1, N, D/2]`` (2-D to 5-D forms accepted as in
+the reference's ``_ensure_4d``). Differences by design: strided q/k/gradient
+views are read in place (no clone for misalignment, no compaction copies in
+backward), any ``eps > 0`` and D in {32, 64, 128, 256} with BF16/FP16/FP32 are
+accepted, and the weight/scale gradients are reduced in a fixed order (no float
+atomics). Nothing here runs on the CPU: the device work is the CUDA library.
+"""
+from typing import Tuple
+
+import torch
+
+from . import _lib
+
+MAX_HEADS = 512
+SUPPORTED_HEAD_DIMS = (32, 64, 128, 256)
+
+_EXPANDED_MSG = "Raw CuTe does not support expanded activations; use the public frontend"
+_CHANNEL_MSG = "Raw CuTe requires channel stride 1; use the public frontend"
+
+
+def _get_compact_strides(shape, strides):
+    """Dense strides that keep the memory order of ``strides`` (stride-0 dims stay 0).
+
+    Same contract as the reference helper (fused_epilogue.py:688-698): dims are
+    ordered by (stride, index) and packed innermost-first.
+    """
+    order = sorted(range(len(shape)), key=lambda i: (int(strides[i]), i))
+    out = list(strides)
+    running = 1
+    for d in order:
+        if strides[d] == 0:
+            out[d] = 0
+        else:
+            out[d] = running
+            running *= shape[d]
+    return tuple(out)
+
+
+def _ensure_4d(t: torch.Tensor) -> torch.Tensor:
+    """sin/cos rank adaptation accepted by the reference op (fused_epilogue.py:22-32)."""
+    if t.ndim == 5:
+        if t.shape[2] == 1:
+            return t.squeeze(2)
+        if t.shape[1] == 1:
+            return t.squeeze(1)
+    elif t.ndim == 3:
+        return t.unsqueeze(1)
+    elif t.ndim == 2:
+        return t.unsqueeze(0).unsqueeze(1)
+    return t
+
+
+def _check_raw(q: torch.Tensor, k: torch.Tensor) -> None:
+    if any(n > 1 and st == 0 for t in (q, k) for n, st in zip(t.shape, t.stride())):
+        raise ValueError(_EXPANDED_MSG)
+    if q.stride(-1) != 1 or k.stride(-1) != 1:
+        raise ValueError(_CHANNEL_MSG)
+
+
+def _check_common(q, k, rmsnorm_weight, scales, sin, cos, eps):
+    if q.ndim != 4 or q.shape != k.shape:
+        raise ValueError("q/k must be matching 4-D [B,H,N,D] tensors")
+    if q.dtype not in _lib.DTYPE_CODES or k.dtype != q.dtype:
+        raise ValueError("q/k must share BF16, FP16, or FP32 dtype")
+    d, h = q.shape[3], q.shape[1]
+    if d not in SUPPORTED_HEAD_DIMS:
+        raise ValueError(f"head dimension must be one of {SUPPORTED_HEAD_DIMS}")
+    if h > MAX_HEADS:
+        raise ValueError(f"at most {MAX_HEADS} heads are supported")
+    if not (eps > 0.0) or eps != eps or eps == float("inf"):
+        raise ValueError("eps must be finite and positive")
+    if tuple(rmsnorm_weight.shape) != (2, 1, d) or scales.numel() != h:
+        raise ValueError("weight must be [2,1,D], log-scales must be [H,1,1]")
+    for value in (rmsnorm_weight, scales, sin, cos):
+        if value.dtype != torch.float32:
+            raise ValueError("weights, log-scales, and sin/cos must be FP32")
+    for t in (k, rmsnorm_weight, scales, sin, cos):
+        if t.device != q.device:
+            raise ValueError("all tensors must share a device")
+    if q.device.type != "cuda":
+        raise ValueError("the prologue kernels run on CUDA devices only")
+
+
+def _table(t: torch.Tensor, B: int, N: int, half: int):
+    """(b, n, j) element strides of a sin/cos table broadcast to [B, 1, N, D/2]."""
+    t4 = _ensure_4d(t)
+    if t4.ndim != 4 or t4.shape[1] != 1 or t4.shape[3] != half:
+        raise ValueError("sin/cos must broadcast over [B,1,N,D/2]")
+    if t4.shape[0] not in (1, B) or t4.shape[2] not in (1, N):
+        raise ValueError("sin/cos must broadcast over [B,1,N,D/2]")
+    sb = t4.stride(0) if t4.shape[0] > 1 else 0
+    sn = t4.stride(2) if t4.shape[2] > 1 else 0
+    return t4, (sb, sn, t4.stride(3))
+
+
+class _DeviceGuard:
+    """Makes ``device`` current for the library call (which launches on it)."""
+
+    def __init__(self, device: torch.device):
+        self.index = device.index
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if self.index is not None and cur != self.index:
+            self.prev = cur
+            torch.cuda.set_device(self.index)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+@torch.library.custom_op("flash_prologue::qknorm_rope_scale_cute", mutates_args=())
+def qknorm_rope_scale_cute_op(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    rmsnorm_weight: torch.Tensor,
+    scales: torch.Tensor,
+    sin: torch.Tensor,
+    cos: torch.Tensor,
+    eps: float = 1e-5,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    _check_raw(q, k)
+    _check_common(q, k, rmsnorm_weight, scales, sin, cos, eps)
+    B, H, N, D = (int(x) for x in q.shape)
+    q_out = torch.empty_strided(q.shape, _get_compact_strides(q.shape, q.stride()),
+                                dtype=q.dtype, device=q.device)
+    k_out = torch.empty_strided(k.shape, _get_compact_strides(k.shape, k.stride()),
+                                dtype=k.dtype, device=k.device)
+    if q.numel() == 0:
+        return q_out, k_out
+    sin4, sin_str = _table(sin, B, N, D // 2)
+    cos4, cos_str = _table(cos, B, N, D // 2)
+    w = rmsnorm_weight.contiguous()
+    s = scales.contiguous()
+    lib = _lib.load()
+    with _DeviceGuard(q.device):
+        status = lib.flash_prologue_fwd(
+            _lib.ptr(q), _lib.strides4(q), _lib.ptr(k), _lib.strides4(k),
+            _lib.ptr(q_out), _lib.strides4(q_out), _lib.ptr(k_out), _lib.strides4(k_out),
+            _lib.ptr(w), _lib.ptr(s),
+            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+            B, H, N, D, float(eps), _lib.DTYPE_CODES[q.dtype], _lib.stream_of(q.device))
+    _lib.check(status, "flash_prologue_fwd")
+    return q_out, k_out
+
+
+@qknorm_rope_scale_cute_op.register_fake
+def _qknorm_rope_scale_cute_fake(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5):
+    _check_raw(q, k)
+    return (
+        torch.empty_strided(q.shape, _get_compact_strides(q.shape, q.stride()),
+                            dtype=q.dtype, device=q.device),
+        torch.empty_strided(k.shape, _get_compact_strides(k.shape, k.stride()),
+                            dtype=k.dtype, device=k.device),
+    )
+
+
+def bwd_workspace_bytes(B: int, H: int, N: int, D: int, dtype: torch.dtype) -> int:
+    """Device workspace (bytes) of the backward launch on the current device."""
+    import ctypes
+    nbytes = ctypes.c_size_t(0)
+    status = _lib.load().flash_prologue_bwd_workspace_size(B, H, N, D, _lib.DTYPE_CODES[dtype],
+                                                           ctypes.byref(nbytes))
+    _lib.check(status, "flash_prologue_bwd_workspace_size")
+    return int(nbytes.value)
+
+
+def _grad_view(g: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    """Upstream gradient as a view the kernel reads in place (channel stride 1)."""
+    if g is None:
+        return torch.zeros((), dtype=like.dtype, device=like.device).expand(like.shape)
+    if g.dtype != like.dtype:
+        g = g.to(like.dtype)
+    if g.stride(-1) != 1 and g.shape[-1] > 1:
+        g = g.contiguous()
+    return g
+
+
+@torch.library.custom_op("flash_prologue::qknorm_rope_scale_cute_backward", mutates_args=())
+def qknorm_rope_scale_cute_backward_op(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    rmsnorm_weight: torch.Tensor,
+    scales: torch.Tensor,
+    sin: torch.Tensor,
+    cos: torch.Tensor,
+    grad_q_out: torch.Tensor,
+    grad_k_out: torch.Tensor,
+    eps: float = 1e-5,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    _check_raw(q, k)
+    _check_common(q, k, rmsnorm_weight, scales, sin, cos, eps)
+    B, H, N, D = (int(x) for x in q.shape)
+    grad_q = torch.empty_strided(q.shape, _get_compact_strides(q.shape, q.stride()),
+                                 dtype=q.dtype, device=q.device)
+    grad_k = torch.empty_strided(k.shape, _get_compact_strides(k.shape, k.stride()),
+                                 dtype=k.dtype, device=k.device)
+    grad_w = torch.empty((2, 1, D), dtype=torch.float32, device=q.device)
+    grad_s = torch.empty((H, 1, 1), dtype=torch.float32, device=q.device)
+    gq = _grad_view(grad_q_out, q)
+    gk = _grad_view(grad_k_out, k)
+    sin4, sin_str = _table(sin, B, N, D // 2)
+    cos4, cos_str = _table(cos, B, N, D // 2)
+    w = rmsnorm_weight.contiguous()
+    s = scales.contiguous()
+    lib = _lib.load()
+    with _DeviceGuard(q.device):
+        nbytes = bwd_workspace_bytes(B, H, N, D, q.dtype) if q.numel() else 0
+        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+        status = lib.flash_prologue_bwd(
+            _lib.ptr(q), _lib.strides4(q), _lib.ptr(k), _lib.strides4(k),
+            _lib.ptr(w), _lib.ptr(s),
+            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+            _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
+            _lib.ptr(grad_q), _lib.strides4(grad_q), _lib.ptr(grad_k), _lib.strides4(grad_k),
+            _lib.ptr(grad_w), _lib.ptr(grad_s),
+            _lib.ptr(workspace), workspace.numel(),
+            B, H, N, D, float(eps), _lib.DTYPE_CODES[q.dtype], _lib.stream_of(q.device))
+    _lib.check(status, "flash_prologue_bwd")
+    return grad_q, grad_k, grad_w, grad_s
+
+
+@qknorm_rope_scale_cute_backward_op.register_fake
+def _qknorm_rope_scale_cute_backward_fake(q, k, rmsnorm_weight, scales, sin, cos, grad_q_out,
+                                          grad_k_out, eps=1e-5):
+    _check_raw(q, k)
+    grad_q = torch.empty_strided(q.shape, _get_compact_strides(q.shape, q.stride()),
+                                 dtype=q.dtype, device=q.device)
+    grad_k = torch.empty_strided(k.shape, _get_compact_strides(k.shape, k.stride()),
+                                 dtype=k.dtype, device=k.device)
+    grad_w = torch.empty((2, 1, q.shape[-1]), device=q.device, dtype=torch.float32)
+    grad_s = torch.empty((q.shape[1], 1, 1), device=q.device, dtype=torch.float32)
+    return grad_q, grad_k, grad_w, grad_s
+
+
+def _setup_context(ctx, inputs, output):
+    q, k, rmsnorm_weight, scales, sin, cos, eps = inputs
+    ctx.save_for_backward(q, k, rmsnorm_weight, scales, sin, cos)
+    ctx.eps = eps
+
+
+def _backward(ctx, grad_q, grad_k):
+    q, k, rmsnorm_weight, scales, sin, cos = ctx.saved_tensors
+    dq, dk, dw, ds = qknorm_rope_scale_cute_backward_op(
+        q, k, rmsnorm_weight, scales, sin, cos, grad_q, grad_k, ctx.eps)
+    return dq, dk, dw, ds, None, None, None
+
+
+torch.library.register_autograd("flash_prologue::qknorm_rope_scale_cute", _backward,
+                                setup_context=_setup_context)

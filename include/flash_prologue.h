@@ -1,0 +1,133 @@
+/*
+ * flash_prologue.h -- C ABI of the B200 (sm_100a) attention-prologue library
+ * (libflash_prologue.so).
+ *
+ * The op ("qknorm_rope_scale") is, per (batch b, head h, position n) row of
+ * length D:
+ *     r      = 1 / sqrt(mean_j(x_j^2) + eps)              (FP32)
+ *     y_j    = (x_j * r) * w[t][j]                        t = 0 for Q, 1 for K
+ *     o_j    = y_j * cos_j - y_{j+D/2} * sin_j            j <  D/2
+ *     o_{j+D/2} = y_{j+D/2} * cos_j + y_j * sin_j
+ *     Q only: o *= exp(scales[h])
+ *     out    = cast(o) to the input dtype (once)
+ * with sin/cos FP32 tables indexed by (b, n) and shared by every head.
+ *
+ * Conventions shared by every entry point:
+ *   - Activations are 4-D [B, H, N, D] views given by a base pointer and four
+ *     int64 strides in ELEMENTS, ordered (b, h, n, d). The d stride must be 1.
+ *     A packed [T, H, D] tensor is passed as B=1, N=T with strides
+ *     (0, stride_h, stride_t, 1), so strided views into a fused QKV buffer
+ *     need no copy.
+ *   - sin/cos are FP32 and indexed [b, n, j] (j < D/2) through three strides
+ *     (b, n, j) in elements; a stride of 0 broadcasts that dimension.
+ *   - rmsnorm_weight is FP32 contiguous [2, 1, D]; scales FP32 contiguous [H].
+ *   - Pointers are device pointers; `stream` is a cudaStream_t (NULL = legacy
+ *     default stream). Every call is asynchronous on `stream`.
+ *   - The library never allocates or frees device memory and never writes an
+ *     input. Callers own every buffer, including backward workspace.
+ *   - Every entry point returns an int status (FLASH_PROLOGUE_OK = 0); the
+ *     message for a status comes from flash_prologue_status_string().
+ *   - dtype codes: 0 = bfloat16, 1 = float16, 2 = float32.
+ */
+#ifndef FLASH_PROLOGUE_H_
+#define FLASH_PROLOGUE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FLASH_PROLOGUE_API __attribute__((visibility("default")))
+#else
+#define FLASH_PROLOGUE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum flash_prologue_status {
+  FLASH_PROLOGUE_OK = 0,
+  FLASH_PROLOGUE_ERR_INVALID_ARGUMENT = 1, /* bad size, null pointer, bad eps */
+  FLASH_PROLOGUE_ERR_UNSUPPORTED = 2,      /* head_dim / dtype not compiled   */
+  FLASH_PROLOGUE_ERR_CHANNEL_STRIDE = 3,   /* d stride != 1                   */
+  FLASH_PROLOGUE_ERR_EXPANDED = 4,         /* stride 0 on a dim of size > 1    */
+  FLASH_PROLOGUE_ERR_WORKSPACE = 5,        /* workspace missing or too small   */
+  FLASH_PROLOGUE_ERR_CUDA = 6,             /* launch or runtime error          */
+  FLASH_PROLOGUE_ERR_ALIGNMENT = 7         /* pointer alignment the path needs */
+};
+
+enum flash_prologue_dtype {
+  FLASH_PROLOGUE_BF16 = 0,
+  FLASH_PROLOGUE_FP16 = 1,
+  FLASH_PROLOGUE_FP32 = 2
+};
+
+/* Human-readable text for a status code (static storage, never NULL). */
+FLASH_PROLOGUE_API const char* flash_prologue_status_string(int status);
+
+/* Library ABI version (major * 100 + minor). */
+FLASH_PROLOGUE_API int flash_prologue_version(void);
+
+/*
+ * Forward prologue.
+ * Replaces the device call of flash_prologue::qknorm_rope_scale_cute
+ * (flash_attn_prologue/fused_epilogue.py:702-815, launch at :794) and its
+ * kernel FusedEpilogueCute.kernel (fused_epilogue.py:245-576).
+ * q_out/k_out may use any strides with d stride 1 (the Python layer passes the
+ * reference's compact-by-permutation strides, fused_epilogue.py:688-698).
+ * Supported: D in {32, 64, 128, 256}; dtype BF16, FP16, FP32; any eps > 0.
+ * B*H*N == 0 returns FLASH_PROLOGUE_OK without a launch.
+ */
+FLASH_PROLOGUE_API int flash_prologue_fwd(const void* q, const int64_t q_strides[4],
+                       const void* k, const int64_t k_strides[4],
+                       void* q_out, const int64_t q_out_strides[4],
+                       void* k_out, const int64_t k_out_strides[4],
+                       const float* rmsnorm_weight, const float* scales,
+                       const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3],
+                       int64_t B, int64_t H, int64_t N, int64_t D,
+                       float eps, int dtype, void* stream);
+
+/*
+ * Bytes of device workspace flash_prologue_bwd needs for this problem on the
+ * current device (the per-CTA partial sums of d rmsnorm_weight and d scales).
+ * No counterpart in the reference, whose backward zeroes its outputs and
+ * accumulates with float atomics (fused_epilogue.py:1403-1404, 1149, 1192-1207).
+ */
+FLASH_PROLOGUE_API int flash_prologue_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D,
+                                      int dtype, size_t* bytes);
+
+/*
+ * Backward prologue: dq, dk (input dtype), d rmsnorm_weight [2*D] FP32 and
+ * d scales [H] FP32, all overwritten (no zeroing needed). The weight/scale
+ * gradients are reduced in a fixed order (per-CTA partials in `workspace`,
+ * then a fixed-order pass), so results are bit-identical run to run on the
+ * same GPU model.
+ * Replaces flash_prologue::qknorm_rope_scale_cute_backward
+ * (fused_epilogue.py:1304-1423, launch at :1411) and
+ * FusedEpilogueBackwardCute.kernel (fused_epilogue.py:907-1207).
+ * Unlike the reference it reads strided q/k/grad views directly instead of
+ * copying them to compact strides first (fused_epilogue.py:1338-1344); the
+ * upstream gradients may also broadcast (stride 0) over b, h or n.
+ * `workspace` must be 16-byte aligned and at least
+ * flash_prologue_bwd_workspace_size() bytes; it needs no initialisation.
+ */
+FLASH_PROLOGUE_API int flash_prologue_bwd(const void* q, const int64_t q_strides[4],
+                       const void* k, const int64_t k_strides[4],
+                       const float* rmsnorm_weight, const float* scales,
+                       const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3],
+                       const void* grad_q_out, const int64_t gq_strides[4],
+                       const void* grad_k_out, const int64_t gk_strides[4],
+                       void* grad_q, const int64_t dq_strides[4],
+                       void* grad_k, const int64_t dk_strides[4],
+                       float* grad_rmsnorm_weight, float* grad_scales,
+                       void* workspace, size_t workspace_bytes,
+                       int64_t B, int64_t H, int64_t N, int64_t D,
+                       float eps, int dtype, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* FLASH_PROLOGUE_H_ */

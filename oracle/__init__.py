@@ -1,0 +1,20 @@
+"""CPU oracle for the attention prologue -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline /
+reference arm may import this package, and only as the checker or the timed CPU
+baseline. The product (``flash_attn_prologue_b200``) never imports it.
+
+* ``native``: the reference's ``native`` backend restated op for op on CPU
+  tensors (flash_attn_prologue/functional.py:49-63 broadcasting, :89-94 math);
+  its backward is autograd through the same ops, exactly as the reference's.
+* ``fp64``: an independent float64 oracle in numpy -- vector-norm RMS and
+  explicit 2x2 rotations as in the reference's tests/test_frontend_api.py:13-32,
+  and a closed-form backward following the identities of the reference's
+  backward kernel (flash_attn_prologue/fused_epilogue.py:1047-1126).
+
+Pinning: tests/golden/ holds outputs and gradients produced by importing the
+reference package itself (tests/golden/make_golden.py); tests/test_oracle_golden.py
+checks both restatements against them.
+"""
+from .native import native_forward, native_forward_backward  # noqa: F401
+from .fp64 import fp64_forward, fp64_backward  # noqa: F401
