@@ -12,9 +12,13 @@ baseline. The product (``flash_attn_prologue_b200``) never imports it.
   and a closed-form backward following the identities of the reference's
   backward kernel (flash_attn_prologue/fused_epilogue.py:1047-1126).
 
+* ``compare``: the output bar -- 1 ulp, or within the FP32 rounding band of
+  the rotation's term magnitudes where its two products nearly cancel.
+
 Pinning: tests/golden/ holds outputs and gradients produced by importing the
 reference package itself (tests/golden/make_golden.py); tests/test_oracle_golden.py
 checks both restatements against them.
 """
 from .native import native_forward, native_forward_backward  # noqa: F401
 from .fp64 import fp64_forward, fp64_backward  # noqa: F401
+from .compare import check_outputs, term_magnitudes  # noqa: F401
