@@ -38,6 +38,8 @@ SIGNATURES = {
                             ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
     "flash_prologue_bwd_workspace_size": ([_i64, _i64, _i64, _i64, ctypes.c_int,
                                            ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "flash_prologue_set_path": ([ctypes.c_int], ctypes.c_int),
+    "flash_prologue_device_error": ([ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
     "flash_prologue_bwd": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,
                             _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
                             _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64,
@@ -71,6 +73,19 @@ def load():
                 fn.restype = restype
             _lib = handle
     return _lib
+
+
+def set_path(mode: int) -> None:
+    """0: bulk-copy pipeline when the layout allows (default); 1: register path only."""
+    check(load().flash_prologue_set_path(int(mode)), "flash_prologue_set_path")
+
+
+def device_error(reset: bool = True) -> int:
+    """Device error word of the pipelined kernels (0 = none); synchronous."""
+    value = ctypes.c_int(0)
+    check(load().flash_prologue_device_error(ctypes.byref(value), int(reset)),
+          "flash_prologue_device_error")
+    return int(value.value)
 
 
 def status_string(status: int) -> str:

@@ -59,7 +59,40 @@ Geometry plan_geometry(int64_t B, int64_t H, int64_t N, int D, bool heads_inner)
   return g;
 }
 
-int64_t persistent_grid(const void* kernel, size_t smem_bytes, int64_t n_items) {
+TmaPlan plan_tma(int64_t B, int64_t H, int64_t N, int D, int dtype, bool heads_inner, int stages) {
+  TmaPlan p{};
+  const int es = dtype == 2 ? 4 : 2;
+  const int rows = kTmaTileBytes / (D * es);
+  p.heads_inner = heads_inner ? 1 : 0;
+  p.stages = stages;
+  int64_t ti;
+  if (heads_inner) {
+    p.inner_ext = H;
+    p.outer_ext = N;
+    ti = 1;
+    while (ti * 2 <= rows && H % (ti * 2) == 0) ti *= 2;
+    if (ti < 4 && ti < H) ti = pow2_floor(H < rows ? H : rows);
+  } else {
+    p.inner_ext = N;
+    p.outer_ext = H;
+    ti = rows >= 16 ? rows / 4 : rows;
+    if (N < ti) {
+      int64_t c = 1;
+      while (c < N) c *= 2;
+      ti = c;
+    }
+  }
+  p.ti = (int)ti;
+  p.log2_ti = log2_exact(ti);
+  p.to = (int)(rows / ti);
+  p.P = heads_inner ? p.to : p.ti;
+  p.n_ib = cdiv(p.inner_ext, p.ti);
+  p.n_ob = cdiv(p.outer_ext, p.to);
+  p.n_tiles = B * p.n_ob * p.n_ib;
+  return p;
+}
+
+int64_t persistent_grid(const void* kernel, size_t smem_bytes, int64_t n_items, int threads) {
   struct Key {
     const void* fn;
     size_t smem;
@@ -85,7 +118,7 @@ int64_t persistent_grid(const void* kernel, size_t smem_bytes, int64_t n_items) 
   if (resident == 0) {
     int sms = 0, per_sm = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem_bytes) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem_bytes) !=
         cudaSuccess)
       return -1;
     if (per_sm < 1) per_sm = 1;
@@ -158,9 +191,49 @@ int common_checks(const void* q, const int64_t* qs, const void* k, const int64_t
   return st;
 }
 
+// 0: automatic (bulk-copy pipeline when the layout allows it), 1: register path only.
+int g_path_mode = 0;
+
+constexpr int kFwdStages = 4;
+constexpr int kBwdStages = 3;
+
+// A streamed input the bulk-copy path can read: 16-byte aligned, rows along
+// the inner dim contiguous (stride D), b and outer strides 16-byte multiples.
+bool tma_tensor_ok(const void* p, const int64_t s[4], int64_t D, size_t es, bool heads_inner,
+                   TmaTensor* out) {
+  if (!aligned16(p) || s[3] != 1) return false;
+  const int64_t s_inner = heads_inner ? s[1] : s[2];
+  const int64_t s_outer = heads_inner ? s[2] : s[1];
+  if (s_inner != D) return false;
+  if (((s[0] * (int64_t)es) & 15) != 0 || ((s_outer * (int64_t)es) & 15) != 0) return false;
+  out->base = static_cast<const char*>(p);
+  out->sb = s[0];
+  out->s_outer = s_outer;
+  return true;
+}
+
+// sin/cos tables the bulk-copy path can read: rows of D/2 contiguous floats.
+bool tma_table_ok(const float* p, const int64_t s[3], int64_t N, int64_t D) {
+  if (!aligned16(p) || s[2] != 1) return false;
+  if (N > 1 && s[1] != D / 2) return false;
+  return ((s[0] * 4) & 15) == 0;
+}
+
 }  // namespace
 
 extern "C" {
+
+FLASH_PROLOGUE_API int flash_prologue_device_error(int* value, int reset) {
+  if (!value) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  return read_device_error(value, reset != 0) == cudaSuccess ? FLASH_PROLOGUE_OK
+                                                             : FLASH_PROLOGUE_ERR_CUDA;
+}
+
+FLASH_PROLOGUE_API int flash_prologue_set_path(int mode) {
+  if (mode != 0 && mode != 1) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  g_path_mode = mode;
+  return FLASH_PROLOGUE_OK;
+}
 
 const char* flash_prologue_status_string(int status) {
   switch (status) {
@@ -196,6 +269,23 @@ int flash_prologue_fwd(const void* q, const int64_t q_strides[4], const void* k,
   const bool vec = view_vec_ok(q, q_strides, es) && view_vec_ok(k, k_strides, es) &&
                    view_vec_ok(q_out, q_out_strides, es) && view_vec_ok(k_out, k_out_strides, es) &&
                    table_vec_ok(sin, sin_strides) && table_vec_ok(cos, cos_strides);
+  const bool heads_inner = heads_inner_layout(q_strides, H, N);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (g_path_mode == 0 && vec) {
+    TmaFwdArgs t{};
+    if (tma_tensor_ok(q, q_strides, D, es, heads_inner, &t.in[0]) &&
+        tma_tensor_ok(k, k_strides, D, es, heads_inner, &t.in[1]) &&
+        tma_table_ok(sin, sin_strides, N, D) && tma_table_ok(cos, cos_strides, N, D)) {
+      t.out[0] = q_out; t.out[1] = k_out;
+      t.so[0] = rows(q_out_strides); t.so[1] = rows(k_out_strides);
+      t.w = rmsnorm_weight; t.scales = scales; t.sin = sin; t.cos = cos;
+      t.sin_b = sin_strides[0]; t.cos_b = cos_strides[0];
+      t.B = B; t.N = N; t.H = (int)H; t.eps = eps;
+      t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kFwdStages);
+      cudaError_t err = launch_fwd_tma(t, dtype, (int)D, s);
+      return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
+    }
+  }
   FwdArgs a{};
   a.x[0] = q; a.x[1] = k; a.y[0] = q_out; a.y[1] = k_out;
   a.sx[0] = rows(q_strides); a.sx[1] = rows(k_strides);
@@ -203,8 +293,8 @@ int flash_prologue_fwd(const void* q, const int64_t q_strides[4], const void* k,
   a.w = rmsnorm_weight; a.scales = scales; a.sin = sin; a.cos = cos;
   a.ssin = table(sin_strides); a.scos = table(cos_strides);
   a.B = B; a.N = N; a.H = (int)H; a.eps = eps;
-  a.g = plan_geometry(B, H, N, (int)D, heads_inner_layout(q_strides, H, N));
-  cudaError_t err = launch_fwd(a, dtype, (int)D, vec, static_cast<cudaStream_t>(stream));
+  a.g = plan_geometry(B, H, N, (int)D, heads_inner);
+  cudaError_t err = launch_fwd(a, dtype, (int)D, vec, s);
   return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
 }
 
@@ -233,6 +323,10 @@ int flash_prologue_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D
       if (st != FLASH_PROLOGUE_OK) return st;
       if (grid > worst) worst = grid;
     }
+    const int64_t tgrid = tma_grid(true, plan_tma(B, H, N, D, dtype, hi != 0, kBwdStages), (int)H,
+                                   (int)D, dtype);
+    if (tgrid <= 0) return FLASH_PROLOGUE_ERR_CUDA;
+    if (tgrid > worst) worst = tgrid;
   }
   *bytes = (size_t)worst * (size_t)(2 * D + H) * sizeof(float);
   return FLASH_PROLOGUE_OK;
@@ -274,9 +368,33 @@ int flash_prologue_bwd(const void* q, const int64_t q_strides[4], const void* k,
                    view_vec_ok(grad_q_out, gq_strides, es) && view_vec_ok(grad_k_out, gk_strides, es) &&
                    view_vec_ok(grad_q, dq_strides, es) && view_vec_ok(grad_k, dk_strides, es) &&
                    table_vec_ok(sin, sin_strides) && table_vec_ok(cos, cos_strides);
+  const bool heads_inner = heads_inner_layout(q_strides, H, N);
+  if (g_path_mode == 0 && vec) {
+    TmaBwdArgs t{};
+    if (tma_tensor_ok(q, q_strides, D, es, heads_inner, &t.in[0]) &&
+        tma_tensor_ok(grad_q_out, gq_strides, D, es, heads_inner, &t.in[1]) &&
+        tma_tensor_ok(k, k_strides, D, es, heads_inner, &t.in[2]) &&
+        tma_tensor_ok(grad_k_out, gk_strides, D, es, heads_inner, &t.in[3]) &&
+        tma_table_ok(sin, sin_strides, N, D) && tma_table_ok(cos, cos_strides, N, D)) {
+      t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kBwdStages);
+      const int64_t tgrid = tma_grid(true, t.p, (int)H, (int)D, dtype);
+      if (tgrid <= 0) return FLASH_PROLOGUE_ERR_CUDA;
+      const size_t tneed = (size_t)tgrid * (size_t)(2 * D + H) * sizeof(float);
+      if (!workspace || workspace_bytes < tneed || !aligned16(workspace))
+        return FLASH_PROLOGUE_ERR_WORKSPACE;
+      t.dx[0] = grad_q; t.dx[1] = grad_k;
+      t.sd[0] = rows(dq_strides); t.sd[1] = rows(dk_strides);
+      t.w = rmsnorm_weight; t.scales = scales; t.sin = sin; t.cos = cos;
+      t.sin_b = sin_strides[0]; t.cos_b = cos_strides[0];
+      t.partials = static_cast<float*>(workspace);
+      t.B = B; t.N = N; t.H = (int)H; t.eps = eps;
+      cudaError_t err = launch_bwd_tma(t, grad_rmsnorm_weight, grad_scales, dtype, (int)D, s);
+      return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
+    }
+  }
   Geometry g;
   int64_t grid;
-  st = bwd_plan(B, H, N, D, dtype, vec, heads_inner_layout(q_strides, H, N), &g, &grid);
+  st = bwd_plan(B, H, N, D, dtype, vec, heads_inner, &g, &grid);
   if (st != FLASH_PROLOGUE_OK) return st;
   const size_t need = (size_t)grid * (size_t)(2 * D + H) * sizeof(float);
   if (!workspace || workspace_bytes < need || !aligned16(workspace)) return FLASH_PROLOGUE_ERR_WORKSPACE;

@@ -271,9 +271,12 @@ cudaError_t launch_bwd(const BwdArgs& a, float* dw, float* ds, int dtype, int D,
   void* args[] = {const_cast<BwdArgs*>(&a)};
   cudaError_t err = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kThreads), args, smem, stream);
   if (err != cudaSuccess) return err;
-  const int C = 2 * D + a.H;
-  prologue_bwd_finalize_kernel<<<(C + 31) / 32, kThreads, 0, stream>>>(a.partials, grid, C, 2 * D,
-                                                                        dw, ds);
+  return launch_bwd_finalize(a.partials, grid, 2 * D + a.H, 2 * D, dw, ds, stream);
+}
+
+cudaError_t launch_bwd_finalize(const float* partials, int64_t G, int C, int two_d, float* dw,
+                                float* ds, cudaStream_t stream) {
+  prologue_bwd_finalize_kernel<<<(C + 31) / 32, kThreads, 0, stream>>>(partials, G, C, two_d, dw, ds);
   return cudaGetLastError();
 }
 

@@ -42,11 +42,79 @@ struct BwdArgs {
   Geometry g;
 };
 
+// ---------------------------------------------------------------------------
+// Bulk-copy (TMA) pipelined path.
+constexpr int kTmaConsumerWarps = 8;                       // 0-3: Q rows, 4-7: K rows
+constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kTmaTileBytes = 8192;                        // per streamed tensor per stage
+
+struct TmaPlan {
+  int heads_inner;      // inner row dim: 1 = heads, 0 = positions
+  int ti, log2_ti;      // rows per tile along the inner dim (power of two)
+  int to;               // rows per tile along the outer dim; ti * to = tile rows
+  int P;                // sin/cos rows per tile
+  int stages;
+  int64_t inner_ext, outer_ext;
+  int64_t n_ib, n_ob, n_tiles;  // tiles = B * n_ob * n_ib, inner block fastest
+};
+
+// One streamed input: rows along the inner dim are contiguous (stride D).
+struct TmaTensor {
+  const char* base;
+  int64_t sb, s_outer;  // element strides of b and of the outer row dim
+};
+
+struct TmaFwdArgs {
+  TmaTensor in[2];      // q, k
+  void* out[2];         // q_out, k_out
+  RowStrides so[2];
+  const float* w;
+  const float* scales;
+  const float* sin;
+  const float* cos;
+  int64_t sin_b, cos_b;  // batch strides of the tables; their n stride is D/2
+  int64_t B, N;
+  int H;
+  float eps;
+  TmaPlan p;
+};
+
+struct TmaBwdArgs {
+  TmaTensor in[4];      // q, grad_q_out, k, grad_k_out
+  void* dx[2];          // dq, dk
+  RowStrides sd[2];
+  const float* w;
+  const float* scales;
+  const float* sin;
+  const float* cos;
+  int64_t sin_b, cos_b;
+  float* partials;      // [grid, 2*D + H]
+  int64_t B, N;
+  int H;
+  float eps;
+  TmaPlan p;
+};
+
+TmaPlan plan_tma(int64_t B, int64_t H, int64_t N, int D, int dtype, bool heads_inner, int stages);
+size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H);
+// Reads (synchronously) and optionally clears the bulk-copy kernels' error word.
+cudaError_t read_device_error(int* value, bool reset);
+int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype);
+cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream);
+cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype, int D,
+                           cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
 // Geometry of a problem (layout-dependent, device-independent).
 Geometry plan_geometry(int64_t B, int64_t H, int64_t N, int D, bool heads_inner);
 
 // Persistent grid for a kernel: min(items, SMs x resident CTAs per SM).
-int64_t persistent_grid(const void* kernel, size_t smem_bytes, int64_t n_items);
+int64_t persistent_grid(const void* kernel, size_t smem_bytes, int64_t n_items,
+                        int threads = kThreads);
+
+// Fixed-order sum of the [G, C] per-CTA partials into dw [two_d] and ds [C - two_d].
+cudaError_t launch_bwd_finalize(const float* partials, int64_t G, int C, int two_d, float* dw,
+                                float* ds, cudaStream_t stream);
 
 // Launchers; return a cudaError_t from the launch.
 cudaError_t launch_fwd(const FwdArgs& a, int dtype, int D, bool vec, cudaStream_t stream);

@@ -1,0 +1,568 @@
+// Bulk-copy (TMA) pipelined forward and backward prologue kernels.
+//
+// CTA = 8 consumer warps + 1 producer warp, two CTAs per SM. A tile is a block
+// of rows of one batch b: `ti` consecutive rows along the "inner" row dim
+// (heads for packed [T,H,D] views, positions for dense [B,H,N,D]), whose rows
+// are contiguous in memory (inner stride == D), times `to` indices of the outer
+// row dim. For every tile the producer warp issues one cp.async.bulk per outer
+// index and input tensor (2 KB - 8 KB each, merged into one when the whole tile
+// is contiguous) plus one per sin/cos table block, completing on the stage's
+// full barrier. Consumer warps 0-3 process the Q rows of the stage, warps 4-7
+// the K rows: each lane owns one 16-element chunk pair of a row (the split-half
+// RoPE partner of each element is in the same lane), reads it from shared
+// memory, and writes its results straight to global memory with 16-byte
+// streaming stores. Stages are recycled through the empty barriers.
+//
+// The arithmetic per row is the one of the register-path kernels
+// (prologue_fwd.cu / prologue_bwd.cu), in the same order, so both paths give
+// bit-identical results.
+#include "prologue_host.h"
+#include "tma_util.cuh"
+
+namespace flash_prologue {
+
+namespace {
+
+template <typename T, int D>
+struct TmaShape {
+  static constexpr int ES = sizeof(T);
+  static constexpr int ROW_BYTES = D * ES;
+  static constexpr int ROWS = kTmaTileBytes / ROW_BYTES;        // rows per tensor per stage
+  static constexpr int L = D / 16;                               // lanes per row
+  static constexpr int LOG2_L = (L == 2) ? 1 : (L == 4) ? 2 : (L == 8) ? 3 : 4;
+  static constexpr int HALF = D / 2;
+  static constexpr int GROUP_THREADS = kTmaConsumerWarps / 2 * 32;  // per tensor
+  static constexpr int ROWS_PER_PASS = GROUP_THREADS / L;
+  static constexpr int PASSES = ROWS / ROWS_PER_PASS;
+  static_assert(PASSES >= 1 && ROWS % ROWS_PER_PASS == 0, "tile geometry");
+};
+
+struct TileCoords {
+  int64_t b, i0, o0;
+  int vi, vo;
+};
+
+__device__ __forceinline__ TileCoords tile_coords(const TmaPlan& p, int64_t tile) {
+  TileCoords tc;
+  const int64_t ib = tile % p.n_ib;
+  const int64_t rest = tile / p.n_ib;
+  const int64_t ob = rest % p.n_ob;
+  tc.b = rest / p.n_ob;
+  tc.i0 = ib * p.ti;
+  tc.o0 = ob * p.to;
+  const int64_t ri = p.inner_ext - tc.i0, ro = p.outer_ext - tc.o0;
+  tc.vi = (int)(ri < p.ti ? ri : p.ti);
+  tc.vo = (int)(ro < p.to ? ro : p.to);
+  return tc;
+}
+
+// Issues the bulk copies of one stage: `nt` streamed tensors then sin and cos.
+// Called by the whole producer warp; lane 0 has already armed the barrier.
+template <int D, int ES>
+__device__ __forceinline__ void issue_stage(const TmaPlan& p, const TmaTensor* in, int nt,
+                                            const float* sin, const float* cos, int64_t sin_b,
+                                            int64_t cos_b, const TileCoords& tc, unsigned char* st,
+                                            int table_bytes, uint64_t* bar, int lane,
+                                            uint64_t pol_stream, uint64_t pol_table) {
+  constexpr int ROW_BYTES = D * ES;
+  const uint32_t run = (uint32_t)tc.vi * ROW_BYTES;  // bytes of one inner run
+  int copies_per_tensor = tc.vo;
+  bool merged[4];
+  for (int t = 0; t < nt; ++t) {
+    merged[t] = tc.vi == p.ti && in[t].s_outer == (int64_t)p.ti * D;
+  }
+  // Copy list: per tensor (merged: one copy of vo runs) then two table copies.
+  int n_copies = 2;
+  for (int t = 0; t < nt; ++t) n_copies += merged[t] ? 1 : copies_per_tensor;
+  const int64_t n_first = p.heads_inner ? tc.o0 : tc.i0;
+  const int np = p.heads_inner ? tc.vo : tc.vi;
+  for (int j = lane; j < n_copies; j += 32) {
+    int jj = j;
+    int t = 0;
+    for (; t < nt; ++t) {
+      const int cnt = merged[t] ? 1 : copies_per_tensor;
+      if (jj < cnt) break;
+      jj -= cnt;
+    }
+    if (t < nt) {
+      const TmaTensor& x = in[t];
+      const int64_t o = tc.o0 + jj;
+      const char* src = x.base + (tc.b * x.sb + o * x.s_outer + tc.i0 * (int64_t)D) * ES;
+      unsigned char* dst = st + t * kTmaTileBytes + jj * p.ti * ROW_BYTES;
+      const uint32_t bytes = merged[t] ? run * (uint32_t)tc.vo : run;
+      bulk_g2s(dst, src, bytes, bar, pol_stream);
+    } else {
+      const bool is_cos = jj == 1;
+      const float* tab = is_cos ? cos : sin;
+      const int64_t tb = is_cos ? cos_b : sin_b;
+      const float* src = tab + tc.b * tb + n_first * (D / 2);
+      unsigned char* dst = st + nt * kTmaTileBytes + (is_cos ? table_bytes : 0);
+      bulk_g2s(dst, src, (uint32_t)np * (D / 2) * 4, bar, pol_table);
+    }
+  }
+}
+
+template <int D, int ES>
+__device__ __forceinline__ uint32_t stage_tx_bytes(const TmaPlan& p, int nt, const TileCoords& tc) {
+  const int np = p.heads_inner ? tc.vo : tc.vi;
+  return (uint32_t)nt * tc.vo * tc.vi * D * ES + 2u * np * (D / 2) * 4;
+}
+
+// 8 values of the activation dtype from shared memory (16 or 32 bytes).
+template <typename T>
+__device__ __forceinline__ void lds_chunk(Chunk<T>& c, const unsigned char* p) {
+  const uint4* p4 = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < Chunk<T>::kWords / 4; ++i) {
+    const uint4 v = p4[i];
+    c.w[4 * i + 0] = v.x; c.w[4 * i + 1] = v.y; c.w[4 * i + 2] = v.z; c.w[4 * i + 3] = v.w;
+  }
+}
+
+// Same as lds_chunk, but never merged with an earlier read of the same row:
+// the backward re-reads its rows for the dx pass instead of keeping every
+// intermediate of the reduction pass live in registers.
+template <typename T>
+__device__ __forceinline__ void lds_chunk_again(Chunk<T>& c, const unsigned char* p) {
+  const uint32_t a = smem_u32(p);
+#pragma unroll
+  for (int i = 0; i < Chunk<T>::kWords / 4; ++i) {
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(c.w[4 * i + 0]), "=r"(c.w[4 * i + 1]), "=r"(c.w[4 * i + 2]), "=r"(c.w[4 * i + 3])
+                 : "r"(a + 16 * i));
+  }
+}
+
+__device__ __forceinline__ void lds_f8(float (&v)[kChunk], const unsigned char* p) {
+  const float4* p4 = reinterpret_cast<const float4*>(p);
+  const float4 a = p4[0], b = p4[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Forward
+template <typename T, int D>
+__global__ void __launch_bounds__(kTmaThreads, 2) prologue_fwd_tma_kernel(const __grid_constant__ TmaFwdArgs a) {
+  using S_ = TmaShape<T, D>;
+  constexpr int HALF = S_::HALF;
+  constexpr int L = S_::L;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int S = a.p.stages;
+  const int table_bytes = a.p.P * HALF * 4;
+  const int stage_bytes = 2 * kTmaTileBytes + 2 * table_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
+  uint64_t* empty = full + S;
+  float* w_s = reinterpret_cast<float*>(empty + S);
+  float* e_s = w_s + 2 * D;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kTmaConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 2 * D; i += kTmaThreads) w_s[i] = a.w[i];
+  for (int i = threadIdx.x; i < a.H; i += kTmaThreads) e_s[i] = (float)exp((double)a.scales[i]);
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp == kTmaConsumerWarps) {  // ---------------- producer ----------------
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_table = policy_evict_last();
+    int k = 0;
+    for (int64_t tile = blockIdx.x; tile < a.p.n_tiles; tile += gridDim.x, ++k) {
+      const int s = k % S;
+      if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
+      const TileCoords tc = tile_coords(a.p, tile);
+      unsigned char* st = smem + s * stage_bytes;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], stage_tx_bytes<D, sizeof(T)>(a.p, 2, tc));
+      __syncwarp();
+      issue_stage<D, sizeof(T)>(a.p, a.in, 2, a.sin, a.cos, a.sin_b, a.cos_b, tc, st, table_bytes,
+                                &full[s], lane, pol_stream, pol_table);
+    }
+    return;
+  }
+
+  // ---------------- consumers: warps 0-3 Q, warps 4-7 K ----------------
+  const int t = warp >> 2;
+  const int gtid = threadIdx.x & (S_::GROUP_THREADS - 1);
+  const int c = gtid & (L - 1);
+  const int slot = gtid >> S_::LOG2_L;
+  const int j0 = c * kChunk;
+  const float* w = w_s + t * D;
+  T* yb = static_cast<T*>(a.out[t]);
+  const RowStrides so = a.so[t];
+  int k = 0;
+  for (int64_t tile = blockIdx.x; tile < a.p.n_tiles; tile += gridDim.x, ++k) {
+    const int s = k % S;
+    if (!mbar_wait(&full[s], (k / S) & 1)) break;
+    const TileCoords tc = tile_coords(a.p, tile);
+    const unsigned char* st = smem + s * stage_bytes;
+    const unsigned char* tile_x = st + t * kTmaTileBytes;
+    const unsigned char* sin_s = st + 2 * kTmaTileBytes;
+    const unsigned char* cos_s = sin_s + table_bytes;
+#pragma unroll
+    for (int pass = 0; pass < S_::PASSES; ++pass) {
+      const int r = pass * S_::ROWS_PER_PASS + slot;
+      const int o_l = r >> a.p.log2_ti;
+      const int i_l = r & (a.p.ti - 1);
+      const bool ok = o_l < tc.vo && i_l < tc.vi;
+      const unsigned char* row = tile_x + r * S_::ROW_BYTES;
+      Chunk<T> x1, x2;
+      lds_chunk(x1, row + j0 * sizeof(T));
+      lds_chunk(x2, row + (HALF + j0) * sizeof(T));
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const float u = chunk_get(x1, j);
+        ss = __fadd_rn(ss, __fmul_rn(u, u));
+      }
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const float u = chunk_get(x2, j);
+        ss = __fadd_rn(ss, __fmul_rn(u, u));
+      }
+      ss = row_sum<L>(ss);
+      if (!ok) continue;
+      const float rr = inv_rms<D>(ss, a.eps);
+      const int p_l = a.p.heads_inner ? o_l : i_l;
+      float sn[kChunk], cs[kChunk];
+      lds_f8(sn, sin_s + (p_l * HALF + j0) * 4);
+      lds_f8(cs, cos_s + (p_l * HALF + j0) * 4);
+      const int64_t h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
+      const int64_t n = a.p.heads_inner ? tc.o0 + o_l : tc.i0 + i_l;
+      float o1[kChunk], o2[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const float y1 = __fmul_rn(__fmul_rn(chunk_get(x1, j), rr), w[j0 + j]);
+        const float y2 = __fmul_rn(__fmul_rn(chunk_get(x2, j), rr), w[HALF + j0 + j]);
+        o1[j] = __fsub_rn(__fmul_rn(y1, cs[j]), __fmul_rn(y2, sn[j]));
+        o2[j] = __fadd_rn(__fmul_rn(y2, cs[j]), __fmul_rn(y1, sn[j]));
+      }
+      if (t == 0) {
+        const float e = e_s[h];
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) { o1[j] = __fmul_rn(o1[j], e); o2[j] = __fmul_rn(o2[j], e); }
+      }
+      Chunk<T> out;
+      T* yp = yb + tc.b * so.b + h * so.h + n * so.n + j0;
+      chunk_set(out, o1);
+      store_stream<T, true>(yp, out);
+      chunk_set(out, o2);
+      store_stream<T, true>(yp + HALF, out);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward
+template <typename T, int D>
+__global__ void __launch_bounds__(kTmaThreads, 2) prologue_bwd_tma_kernel(const __grid_constant__ TmaBwdArgs a) {
+  using S_ = TmaShape<T, D>;
+  constexpr int HALF = S_::HALF;
+  constexpr int L = S_::L;
+  constexpr int LOG2_L = S_::LOG2_L;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int S = a.p.stages;
+  const int table_bytes = a.p.P * HALF * 4;
+  const int stage_bytes = 4 * kTmaTileBytes + 2 * table_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
+  uint64_t* empty = full + S;
+  float* w_s = reinterpret_cast<float*>(empty + S);   // [2 * D]
+  float* e_s = w_s + 2 * D;                            // [H]
+  float* ds_s = e_s + a.H;                             // [4][H]  (Q warps)
+  float* dw_s = ds_s + 4 * a.H;                        // [8][D]
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kTmaConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 2 * D; i += kTmaThreads) w_s[i] = a.w[i];
+  for (int i = threadIdx.x; i < a.H; i += kTmaThreads) e_s[i] = (float)exp((double)a.scales[i]);
+  for (int i = threadIdx.x; i < 4 * a.H; i += kTmaThreads) ds_s[i] = 0.f;
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp == kTmaConsumerWarps) {  // ---------------- producer ----------------
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_table = policy_evict_last();
+    int k = 0;
+    for (int64_t tile = blockIdx.x; tile < a.p.n_tiles; tile += gridDim.x, ++k) {
+      const int s = k % S;
+      if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
+      const TileCoords tc = tile_coords(a.p, tile);
+      unsigned char* st = smem + s * stage_bytes;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], stage_tx_bytes<D, sizeof(T)>(a.p, 4, tc));
+      __syncwarp();
+      issue_stage<D, sizeof(T)>(a.p, a.in, 4, a.sin, a.cos, a.sin_b, a.cos_b, tc, st, table_bytes,
+                                &full[s], lane, pol_stream, pol_table);
+    }
+    return;
+  }
+
+  // ---------------- consumers: warps 0-3 Q, warps 4-7 K ----------------
+  const int t = warp >> 2;
+  const int gtid = threadIdx.x & (S_::GROUP_THREADS - 1);
+  const int c = gtid & (L - 1);
+  const int slot = gtid >> LOG2_L;
+  const int j0 = c * kChunk;
+  const float* w = w_s + t * D;
+  T* db = static_cast<T*>(a.dx[t]);
+  const RowStrides sd = a.sd[t];
+
+  // Lanes (within a warp) that hold rows of the same head differ only in the
+  // chunk bits and in the lane bits [ps_lo, ps_hi).
+  const int warp_slot_bits = 5 - LOG2_L;
+  int ps_lo, ps_hi;
+  if (a.p.heads_inner) {
+    ps_lo = LOG2_L + min(a.p.log2_ti, warp_slot_bits);
+    ps_hi = 5;
+  } else {
+    ps_lo = LOG2_L;
+    ps_hi = LOG2_L + min(a.p.log2_ti, warp_slot_bits);
+  }
+  const bool ds_writer = ((lane & ((1 << ps_hi) - 1)) >> ps_lo) == 0 && c == 0;
+
+  float acc1[kChunk], acc2[kChunk];
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) { acc1[j] = 0.f; acc2[j] = 0.f; }
+
+  int k = 0;
+  for (int64_t tile = blockIdx.x; tile < a.p.n_tiles; tile += gridDim.x, ++k) {
+    const int s = k % S;
+    if (!mbar_wait(&full[s], (k / S) & 1)) break;
+    const TileCoords tc = tile_coords(a.p, tile);
+    const unsigned char* st = smem + s * stage_bytes;
+    const unsigned char* tile_x = st + (2 * t) * kTmaTileBytes;
+    const unsigned char* tile_g = st + (2 * t + 1) * kTmaTileBytes;
+    const unsigned char* sin_s = st + 4 * kTmaTileBytes;
+    const unsigned char* cos_s = sin_s + table_bytes;
+#pragma unroll 1
+    for (int pass = 0; pass < S_::PASSES; ++pass) {
+      const int r = pass * S_::ROWS_PER_PASS + slot;
+      const int o_l = r >> a.p.log2_ti;
+      const int i_l = r & (a.p.ti - 1);
+      const bool ok = o_l < tc.vo && i_l < tc.vi;
+      Chunk<T> x1, x2, g1, g2;
+      if (ok) {
+        const unsigned char* xr = tile_x + r * S_::ROW_BYTES;
+        const unsigned char* gr = tile_g + r * S_::ROW_BYTES;
+        lds_chunk(x1, xr + j0 * sizeof(T));
+        lds_chunk(x2, xr + (HALF + j0) * sizeof(T));
+        lds_chunk(g1, gr + j0 * sizeof(T));
+        lds_chunk(g2, gr + (HALF + j0) * sizeof(T));
+      } else {
+#pragma unroll
+        for (int q = 0; q < Chunk<T>::kWords; ++q) { x1.w[q] = 0; x2.w[q] = 0; g1.w[q] = 0; g2.w[q] = 0; }
+      }
+      const int p_l = a.p.heads_inner ? o_l : i_l;
+      float sn[kChunk], cs[kChunk];
+      if (ok) {
+        lds_f8(sn, sin_s + (p_l * HALF + j0) * 4);
+        lds_f8(cs, cos_s + (p_l * HALF + j0) * 4);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) { sn[j] = 0.f; cs[j] = 0.f; }
+      }
+      const int64_t h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
+      const int64_t n = a.p.heads_inner ? tc.o0 + o_l : tc.i0 + i_l;
+      const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
+
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        float v = chunk_get(x1, j); ss = __fadd_rn(ss, __fmul_rn(v, v));
+      }
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        float v = chunk_get(x2, j); ss = __fadd_rn(ss, __fmul_rn(v, v));
+      }
+      ss = row_sum<L>(ss);
+      const float rr = inv_rms<D>(ss, a.eps);
+
+      // Pass 1: reductions (d w partials, sum(dn w n), d scales).
+      float dsum = 0.f, ds_part = 0.f;
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const float n1 = chunk_get(x1, j) * rr, n2 = chunk_get(x2, j) * rr;
+        const float gg1 = chunk_get(g1, j) * e, gg2 = chunk_get(g2, j) * e;
+        const float d1 = gg1 * cs[j] + gg2 * sn[j];
+        const float d2 = gg2 * cs[j] - gg1 * sn[j];
+        const float wa = w[j0 + j], wb = w[HALF + j0 + j];
+        if (t == 0) {
+          const float ya = n1 * wa, yb = n2 * wb;
+          ds_part += gg1 * (ya * cs[j] - yb * sn[j]) + gg2 * (yb * cs[j] + ya * sn[j]);
+        }
+        acc1[j] += d1 * n1;
+        acc2[j] += d2 * n2;
+        dsum += d1 * wa * n1 + d2 * wb * n2;
+      }
+      dsum = row_sum<L>(dsum);
+      if (t == 0) {
+        ds_part = row_sum<L>(ds_part);
+        for (int bit = ps_lo; bit < ps_hi; ++bit)
+          ds_part = __fadd_rn(ds_part, __shfl_xor_sync(0xffffffffu, ds_part, 1 << bit));
+        if (ds_writer && h < a.H) ds_s[warp * a.H + h] += ds_part;
+      }
+      if (!ok) continue;
+      // Pass 2: dx = r (dn w - n mean(dn w n)), with dn recomputed from the
+      // rows re-read from shared memory (same expressions as pass 1).
+      const float m = dsum * (1.0f / (float)D);
+      {
+        const unsigned char* xr = tile_x + r * S_::ROW_BYTES;
+        const unsigned char* gr = tile_g + r * S_::ROW_BYTES;
+        lds_chunk_again(x1, xr + j0 * sizeof(T));
+        lds_chunk_again(x2, xr + (HALF + j0) * sizeof(T));
+        lds_chunk_again(g1, gr + j0 * sizeof(T));
+        lds_chunk_again(g2, gr + (HALF + j0) * sizeof(T));
+      }
+      float o1[kChunk], o2[kChunk];
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const float n1 = chunk_get(x1, j) * rr, n2 = chunk_get(x2, j) * rr;
+        const float gg1 = chunk_get(g1, j) * e, gg2 = chunk_get(g2, j) * e;
+        const float d1 = gg1 * cs[j] + gg2 * sn[j];
+        const float d2 = gg2 * cs[j] - gg1 * sn[j];
+        o1[j] = rr * (d1 * w[j0 + j] - n1 * m);
+        o2[j] = rr * (d2 * w[HALF + j0 + j] - n2 * m);
+      }
+      Chunk<T> out;
+      T* dp = db + tc.b * sd.b + h * sd.h + n * sd.n + j0;
+      chunk_set(out, o1);
+      store_stream<T, true>(dp, out);
+      chunk_set(out, o2);
+      store_stream<T, true>(dp + HALF, out);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // d w: combine lanes holding the same chunk (fixed xor order), then warps.
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) {
+#pragma unroll
+    for (int o = L; o < 32; o <<= 1) {
+      acc1[j] = __fadd_rn(acc1[j], __shfl_xor_sync(0xffffffffu, acc1[j], o));
+      acc2[j] = __fadd_rn(acc2[j], __shfl_xor_sync(0xffffffffu, acc2[j], o));
+    }
+  }
+  if (lane < L) {
+    float* dst = dw_s + warp * D;
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      dst[j0 + j] = acc1[j];
+      dst[HALF + j0 + j] = acc2[j];
+    }
+  }
+  consumer_sync(kTmaConsumerWarps * 32);
+  const int C = 2 * D + a.H;
+  float* out = a.partials + (int64_t)blockIdx.x * C;
+  for (int col = threadIdx.x; col < C; col += kTmaConsumerWarps * 32) {
+    float v = 0.f;
+    if (col < D) {
+#pragma unroll
+      for (int w8 = 0; w8 < 4; ++w8) v = __fadd_rn(v, dw_s[w8 * D + col]);
+    } else if (col < 2 * D) {
+#pragma unroll
+      for (int w8 = 4; w8 < 8; ++w8) v = __fadd_rn(v, dw_s[w8 * D + (col - D)]);
+    } else {
+#pragma unroll
+      for (int w8 = 0; w8 < 4; ++w8) v = __fadd_rn(v, ds_s[w8 * a.H + (col - 2 * D)]);
+    }
+    out[col] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+
+cudaError_t read_device_error(int* value, bool reset) {
+  cudaError_t err = cudaMemcpyFromSymbol(value, g_device_error, sizeof(int));
+  if (err != cudaSuccess || !reset) return err;
+  const int zero = 0;
+  return cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+}
+
+size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H) {
+  const size_t table = (size_t)p.P * (D / 2) * 4;
+  const size_t stage = (size_t)n_tensors * kTmaTileBytes + 2 * table;
+  size_t extra = (size_t)2 * p.stages * sizeof(uint64_t) + (size_t)(2 * D + H) * 4;
+  if (n_tensors == 4) extra += (size_t)(4 * H + 8 * D) * 4;
+  return p.stages * stage + extra;
+}
+
+template <typename T, int D>
+static const void* fwd_tma_ptr() { return reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D>); }
+template <typename T, int D>
+static const void* bwd_tma_ptr() { return reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D>); }
+
+static const void* tma_kernel_for(bool bwd, int dtype, int D) {
+#define FP_TMA_CASE(T)                                                    \
+  switch (D) {                                                            \
+    case 32: return bwd ? bwd_tma_ptr<T, 32>() : fwd_tma_ptr<T, 32>();     \
+    case 64: return bwd ? bwd_tma_ptr<T, 64>() : fwd_tma_ptr<T, 64>();     \
+    case 128: return bwd ? bwd_tma_ptr<T, 128>() : fwd_tma_ptr<T, 128>();  \
+    case 256: return bwd ? bwd_tma_ptr<T, 256>() : fwd_tma_ptr<T, 256>();  \
+    default: return nullptr;                                              \
+  }
+  switch (dtype) {
+    case 0: FP_TMA_CASE(__nv_bfloat16)
+    case 1: FP_TMA_CASE(__half)
+    case 2: FP_TMA_CASE(float)
+    default: return nullptr;
+  }
+#undef FP_TMA_CASE
+}
+
+static cudaError_t prepare_kernel(const void* fn, size_t smem) {
+  // Opt in to more than 48 KB of dynamic shared memory (idempotent, cheap).
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype) {
+  const void* fn = tma_kernel_for(bwd, dtype, D);
+  if (!fn) return -1;
+  const size_t smem = tma_smem_bytes(p, D, bwd ? 4 : 2, H);
+  if (prepare_kernel(fn, smem) != cudaSuccess) return -1;
+  return persistent_grid(fn, smem, p.n_tiles, kTmaThreads);
+}
+
+cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream) {
+  const void* fn = tma_kernel_for(false, dtype, D);
+  if (!fn) return cudaErrorInvalidValue;
+  const size_t smem = tma_smem_bytes(a.p, D, 2, a.H);
+  cudaError_t err = prepare_kernel(fn, smem);
+  if (err != cudaSuccess) return err;
+  const int64_t grid = persistent_grid(fn, smem, a.p.n_tiles, kTmaThreads);
+  if (grid <= 0) return cudaErrorInvalidConfiguration;
+  void* args[] = {const_cast<TmaFwdArgs*>(&a)};
+  return cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kTmaThreads), args, smem, stream);
+}
+
+cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype, int D,
+                           cudaStream_t stream) {
+  const void* fn = tma_kernel_for(true, dtype, D);
+  if (!fn) return cudaErrorInvalidValue;
+  const size_t smem = tma_smem_bytes(a.p, D, 4, a.H);
+  cudaError_t err = prepare_kernel(fn, smem);
+  if (err != cudaSuccess) return err;
+  const int64_t grid = persistent_grid(fn, smem, a.p.n_tiles, kTmaThreads);
+  if (grid <= 0) return cudaErrorInvalidConfiguration;
+  void* args[] = {const_cast<TmaBwdArgs*>(&a)};
+  err = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kTmaThreads), args, smem, stream);
+  if (err != cudaSuccess) return err;
+  return launch_bwd_finalize(a.partials, grid, 2 * D + a.H, 2 * D, dw, ds, stream);
+}
+
+}  // namespace flash_prologue

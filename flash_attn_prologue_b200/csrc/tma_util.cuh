@@ -1,0 +1,90 @@
+// Bulk-copy (TMA) and mbarrier helpers for sm_100a, written as inline PTX.
+//
+// Every wait is bounded: after kMaxWaitTries suspended polls (a few seconds in
+// total) the waiter records kDeviceErrorTimeout in the library's device error
+// word and gives up, so a protocol bug ends the kernel instead of hanging the
+// GPU. flash_prologue_device_error() reads (and optionally clears) the word.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace flash_prologue {
+
+constexpr int kDeviceErrorTimeout = 1;
+constexpr uint32_t kMaxWaitTries = 1u << 22;  // x suspend hint below: about 4 s
+constexpr uint32_t kSuspendHintNs = 1000;
+
+// Device error word of the bulk-copy kernels (0 = no error). One definition
+// per translation unit that includes this header (the library is built
+// without relocatable device code); only prologue_tma.cu includes it.
+static __device__ int g_device_error = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Makes barrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;"
+               ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Waits for the phase with the given parity to complete. Returns false (and
+// records a device error) if it did not within the bound.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  for (uint32_t i = 0; i < kMaxWaitTries; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done) : "r"(a), "r"(parity), "r"(kSuspendHintNs) : "memory");
+    if (done) return true;
+  }
+  atomicExch(&g_device_error, kDeviceErrorTimeout);
+  return false;
+}
+
+// L2 eviction policies for bulk copies.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Global -> shared bulk copy (no multicast) completing on `bar` with a byte
+// count. Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Barrier over the consumer warps only (the producer warp does not take part).
+__device__ __forceinline__ void consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+}  // namespace flash_prologue

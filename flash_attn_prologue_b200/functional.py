@@ -94,7 +94,9 @@ def qknorm_rope_scale(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5, *, backe
         out_q, out_k = torch.ops.flash_prologue.qknorm_rope_scale_cute(
             q4, k4, rmsnorm_weight, scales, s4, c4, eps)
         if q.ndim == 3:
-            return out_q[0].permute(1, 0, 2), out_k[0].permute(1, 0, 2)
+            # squeeze (a view in both directions), not out[0]: the backward of a
+            # select would allocate zeros and scatter-copy every gradient.
+            return out_q.squeeze(0).permute(1, 0, 2), out_k.squeeze(0).permute(1, 0, 2)
         return out_q, out_k
 
     def transform(x, weight):

@@ -126,6 +126,24 @@ FLASH_PROLOGUE_API int flash_prologue_bwd(const void* q, const int64_t q_strides
                        int64_t B, int64_t H, int64_t N, int64_t D,
                        float eps, int dtype, void* stream);
 
+/*
+ * Kernel path selection (process-wide, not thread-safe; for tests and tuning).
+ * mode 0 (default): the bulk-copy (TMA) pipelined kernels whenever the views
+ * allow them (16-byte aligned, rows contiguous along the inner row dim, sin/cos
+ * rows contiguous), else the register-path kernels; mode 1: register path
+ * only. Both paths compute bit-identical results.
+ * No counterpart in the reference (which has a single kernel per op).
+ */
+FLASH_PROLOGUE_API int flash_prologue_set_path(int mode);
+
+/*
+ * Reads the device error word of the pipelined kernels (0 = none; 1 = a
+ * bounded barrier wait gave up, which means the results of that launch are
+ * invalid). Synchronous (copies from the device); clears the word if `reset`.
+ * No counterpart in the reference (which has no device-side waits).
+ */
+FLASH_PROLOGUE_API int flash_prologue_device_error(int* value, int reset);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -249,3 +249,55 @@ def test_backward_bit_reproducible():
         again = op(q4, k4, w, s, s4, c4, g4q, g4k, 1e-5)
         for a, b in zip(first, again):
             assert torch.equal(a, b)
+
+
+# ----------------------------------------------------------------------------
+# The two kernel paths (bulk-copy pipeline and register path) compute the same
+# per-row arithmetic: outputs and dq/dk must be bit-identical; the parameter
+# gradients differ only in the (fixed) grouping of their partial sums.
+
+def _run_both_paths(args, gq, gk):
+    from flash_attn_prologue_b200 import _lib
+    results = []
+    try:
+        for mode in (0, 1):
+            _lib.set_path(mode)
+            a = [t.detach().requires_grad_(i < 4) for i, t in enumerate(args)]
+            out = qknorm_rope_scale(*a, backend="cute")
+            grads = torch.autograd.grad(out, a[:4], (gq, gk))
+            results.append((out, grads))
+    finally:
+        _lib.set_path(0)
+    assert _lib.device_error(reset=True) == 0
+    return results
+
+
+@pytest.mark.parametrize("layout", ["qkv_packed", "packed", "dense"])
+@pytest.mark.parametrize("d", [32, 64, 128, 256])
+def test_bulk_copy_and_register_paths_agree(layout, d):
+    h, t = 8, 300
+    g = torch.Generator(device="cuda").manual_seed(d)
+    if layout == "qkv_packed":
+        buf = torch.randn(t, 3, h, d, generator=g, device="cuda").to(torch.bfloat16)
+        q, k = buf[:, 0], buf[:, 1]
+        tab = (t, d // 2)
+    elif layout == "packed":
+        q, k = (torch.randn(t, h, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(2))
+        tab = (t, d // 2)
+    else:
+        q, k = (torch.randn(2, h, t, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(2))
+        tab = (2, t, d // 2)
+    ang = torch.randn(tab, generator=g, device="cuda")
+    w = 1 + 0.2 * torch.randn(2, 1, d, generator=g, device="cuda")
+    s = 0.2 * torch.randn(h, 1, 1, generator=g, device="cuda")
+    gq = torch.randn(q.shape, generator=g, device="cuda").to(torch.bfloat16)
+    gk = torch.randn(k.shape, generator=g, device="cuda").to(torch.bfloat16)
+    (o0, g0), (o1, g1) = _run_both_paths((q, k, w, s, ang.sin(), ang.cos()), gq, gk)
+    assert torch.equal(o0[0], o1[0]) and torch.equal(o0[1], o1[1])
+    assert torch.equal(g0[0], g1[0]) and torch.equal(g0[1], g1[1])
+    assert rel_err(g0[2], g1[2]) < 1e-5 and rel_err(g0[3], g1[3]) < 1e-5
+
+
+def test_no_device_wait_timeouts():
+    from flash_attn_prologue_b200 import _lib
+    assert _lib.device_error(reset=True) == 0
