@@ -183,6 +183,8 @@ int common_checks(const void* q, const int64_t* qs, const void* k, const int64_t
   if (!(eps > 0.f) || !isfinite(eps)) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   if (dtype < 0 || dtype > 2 || !supported_dim(D)) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
   if (H > kMaxHeads) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
+  // Work-cursor digits are 32-bit.
+  if (B >= (int64_t(1) << 31) || N >= (int64_t(1) << 31)) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
   if (!qs || !ks || !sins || !coss) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   if (B * H * N == 0) return FLASH_PROLOGUE_OK;
   if (!q || !k || !w || !sc || !sin || !cos) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
@@ -311,6 +313,7 @@ int flash_prologue_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D
   *bytes = 0;
   if (B < 0 || H < 0 || N < 0) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   if (dtype < 0 || dtype > 2 || !supported_dim(D) || H > kMaxHeads) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
+  if (B >= (int64_t(1) << 31) || N >= (int64_t(1) << 31)) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
   if (B * H * N == 0) return FLASH_PROLOGUE_OK;
   // The grid (and so the workspace) is the largest of the layouts and vector
   // widths the call may pick, so one size serves every stride pattern.

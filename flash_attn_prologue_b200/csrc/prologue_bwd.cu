@@ -6,7 +6,9 @@
 //   r  = 1/sqrt(mean(x^2)+eps),  n = x*r
 //   g' = g*e
 //   dn_j = g'_j cos_j + g'_{j+D/2} sin_j,  dn_{j+D/2} = g'_{j+D/2} cos_j - g'_j sin_j
-//   d scales[h]   += sum_j g'_j * rot(n*w)_j           (Q rows only)
+//   d scales[h]   += sum_j g'_j * rot(n*w)_j  =  sum_j dn_j w_j n_j   (Q rows only;
+//                    the rotation is orthogonal, so the reference's separate dot
+//                    product equals the one dx needs anyway)
 //   d w[t][j]     += dn_j * n_j
 //   dx_j = r * (dn_j w_j - n_j * sum_i(dn_i w_i n_i) / D)
 // The reference accumulates the two parameter gradients with float atomics
@@ -69,10 +71,9 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
 #pragma unroll
   for (int j = 0; j < kChunk; ++j) { acc1[j] = 0.f; acc2[j] = 0.f; }
 
-  for (int64_t item = blockIdx.x; item < a.g.n_items; item += gridDim.x) {
-    int ti;
-    int64_t b, pb, hg;
-    item_coords(a.g, item, ti, b, pb, hg);
+  Cursor4 cur;
+  for (cur.init(blockIdx.x, a.g.radix); cur.d[3] < a.B; cur.advance(a.g.radix)) {
+    const int64_t pb = cur.d[1], hg = cur.d[2], b = cur.d[3];
     const int64_t n = pb * PS + ps;
     const bool pos_ok = n < a.N;
 
@@ -101,62 +102,23 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
         for (int k = 0; k < Chunk<T>::kWords; ++k) { x1.w[k] = 0; x2.w[k] = 0; g1.w[k] = 0; g2.w[k] = 0; }
       }
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
-
-      float ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        float v = chunk_get(x1, j); ss = __fadd_rn(ss, __fmul_rn(v, v));
-      }
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        float v = chunk_get(x2, j); ss = __fadd_rn(ss, __fmul_rn(v, v));
-      }
-      ss = row_sum<L>(ss);
-      const float r = inv_rms<D>(ss, a.eps);
-
-      float dsum = 0.f, ds_part = 0.f;
-      float dn1[kChunk], dn2[kChunk];
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float n1 = chunk_get(x1, j) * r, n2 = chunk_get(x2, j) * r;
-        const float gg1 = chunk_get(g1, j) * e, gg2 = chunk_get(g2, j) * e;
-        const float d1 = gg1 * cs[j] + gg2 * sn[j];
-        const float d2 = gg2 * cs[j] - gg1 * sn[j];
-        const float wa = w[j0 + j], wb = w[HALF + j0 + j];
-        if (t == 0) {
-          const float ya = n1 * wa, yb = n2 * wb;
-          ds_part += gg1 * (ya * cs[j] - yb * sn[j]) + gg2 * (yb * cs[j] + ya * sn[j]);
-        }
-        acc1[j] += d1 * n1;
-        acc2[j] += d2 * n2;
-        dsum += d1 * wa * n1 + d2 * wb * n2;
-        dn1[j] = d1;
-        dn2[j] = d2;
-      }
-      dsum = row_sum<L>(dsum);
+      const float r = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
+      float dnw1[kChunk], dnw2[kChunk];
+      const float dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, r, e, t == 0, w + j0,
+                                                    w + HALF + j0, sn, cs, acc1, acc2, dnw1, dnw2));
       if (t == 0) {
-        // d scales: reduce over the row's lanes and the warp's position slots.
-        ds_part = row_sum<L>(ds_part);
+        // d scales: the row's sum(dn w n), reduced over the warp's position slots.
+        float v = dsum;
         for (int bit = ps_lo; bit < ps_hi; ++bit)
-          ds_part = __fadd_rn(ds_part, __shfl_xor_sync(0xffffffffu, ds_part, 1 << bit));
-        if (ds_writer && h < a.H) ds_s[warp * a.H + h] += ds_part;
+          v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1 << bit));
+        if (ds_writer && h < a.H) ds_s[warp * a.H + h] += v;
       }
-
       if (!ok) continue;
-      const float m = dsum * (1.0f / (float)D);
-      float o1[kChunk], o2[kChunk];
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float n1 = chunk_get(x1, j) * r, n2 = chunk_get(x2, j) * r;
-        o1[j] = r * (dn1[j] * w[j0 + j] - n1 * m);
-        o2[j] = r * (dn2[j] * w[HALF + j0 + j] - n2 * m);
-      }
-      Chunk<T> out;
+      Chunk<T> out1, out2;
+      bwd_lane_dx(x1, x2, r, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
       T* dp = db + b * sd.b + (int64_t)h * sd.h + n * sd.n + j0;
-      chunk_set(out, o1);
-      store_stream<T, VEC>(dp, out);
-      chunk_set(out, o2);
-      store_stream<T, VEC>(dp + HALF, out);
+      store_stream<T, VEC>(dp, out1);
+      store_stream<T, VEC>(dp + HALF, out2);
     }
   }
 
@@ -268,7 +230,9 @@ cudaError_t launch_bwd(const BwdArgs& a, float* dw, float* ds, int dtype, int D,
   int64_t grid = persistent_grid(fn, smem, a.g.n_items);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
   grid = even_grid(grid, a.g.n_items);
-  void* args[] = {const_cast<BwdArgs*>(&a)};
+  BwdArgs launch_args = a;
+  launch_args.g.radix = make_radix(2, a.g.n_pos_blocks, a.g.n_head_groups, grid);
+  void* args[] = {&launch_args};
   cudaError_t err = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kThreads), args, smem, stream);
   if (err != cudaSuccess) return err;
   return launch_bwd_finalize(a.partials, grid, 2 * D + a.H, 2 * D, dw, ds, stream);

@@ -39,6 +39,47 @@ struct TableStrides {  // element strides of a sin/cos table indexed [b, n, j]
   int64_t b, n, j;
 };
 
+// Mixed-radix position of a persistent CTA's work item: digit 0 fastest,
+// digit 3 unbounded. CTAs advance by the grid size without divisions: the
+// digits of the grid size are precomputed on the host (make_radix).
+struct Radix4 {
+  int32_t ext[3];   // extents of digits 0..2
+  int32_t step[4];  // digits of the grid size
+};
+
+struct Cursor4 {
+  int32_t d[4];
+  __device__ __forceinline__ void init(int32_t idx, const Radix4& r) {
+    d[0] = idx % r.ext[0];
+    idx /= r.ext[0];
+    d[1] = idx % r.ext[1];
+    idx /= r.ext[1];
+    d[2] = idx % r.ext[2];
+    d[3] = idx / r.ext[2];
+  }
+  __device__ __forceinline__ void advance(const Radix4& r) {
+    d[0] += r.step[0];
+    d[1] += r.step[1];
+    d[2] += r.step[2];
+    d[3] += r.step[3];
+    if (d[0] >= r.ext[0]) { d[0] -= r.ext[0]; ++d[1]; }
+    if (d[1] >= r.ext[1]) { d[1] -= r.ext[1]; ++d[2]; }
+    if (d[2] >= r.ext[2]) { d[2] -= r.ext[2]; ++d[3]; }
+  }
+};
+
+// Digits of `stride` in the radix (e0, e1, e2, unbounded). Every extent and
+// the stride are below 2^31 (checked by the C-ABI layer).
+inline Radix4 make_radix(int64_t e0, int64_t e1, int64_t e2, int64_t stride) {
+  Radix4 r;
+  r.ext[0] = (int32_t)e0; r.ext[1] = (int32_t)e1; r.ext[2] = (int32_t)e2;
+  r.step[0] = (int32_t)(stride % e0); stride /= e0;
+  r.step[1] = (int32_t)(stride % e1); stride /= e1;
+  r.step[2] = (int32_t)(stride % e2);
+  r.step[3] = (int32_t)(stride / e2);
+  return r;
+}
+
 // Launch geometry shared by host planning and kernels.
 struct Geometry {
   int log2_l;          // lanes per row = D / 16
@@ -49,6 +90,7 @@ struct Geometry {
   int64_t n_pos_blocks;
   int64_t n_head_groups;
   int64_t n_items;     // 2 (tensors) * B * n_head_groups * n_pos_blocks
+  Radix4 radix;        // digits (tensor, position block, head group) + batch
 };
 
 // ---------------------------------------------------------------------------
@@ -185,6 +227,99 @@ __device__ __forceinline__ float inv_rms(float sumsq, float eps) {
   return __frcp_rn(__fsqrt_rn(__fadd_rn(mean, eps)));
 }
 
+// ---------------------------------------------------------------------------
+// Per-row arithmetic shared by the register-path and the bulk-copy kernels (so
+// both give bit-identical results). A lane holds the chunk pair
+// x1 = x[j0 .. j0+8), x2 = x[D/2+j0 .. D/2+j0+8) of its row.
+
+// Lane-partial sum of squares. For 16-bit inputs x*x is exact in FP32, so the
+// fused multiply-add rounds exactly like "square, then add".
+template <typename T>
+__device__ __forceinline__ float lane_sumsq(const Chunk<T>& x1, const Chunk<T>& x2) {
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) {
+    const float u = chunk_get(x1, j);
+    ss = (sizeof(T) == 2) ? fmaf(u, u, ss) : __fadd_rn(ss, __fmul_rn(u, u));
+  }
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) {
+    const float u = chunk_get(x2, j);
+    ss = (sizeof(T) == 2) ? fmaf(u, u, ss) : __fadd_rn(ss, __fmul_rn(u, u));
+  }
+  return ss;
+}
+
+// Forward outputs of one lane: normed = (x * r) * w, rotated, times e for Q.
+// Every product and sum rounds separately, as in the eager formulation.
+template <typename T>
+__device__ __forceinline__ void fwd_lane(const Chunk<T>& x1, const Chunk<T>& x2, float r,
+                                         const float* wa, const float* wb, const float (&sn)[kChunk],
+                                         const float (&cs)[kChunk], bool scale, float e,
+                                         Chunk<T>& out1, Chunk<T>& out2) {
+  float o1[kChunk], o2[kChunk];
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) {
+    const float y1 = __fmul_rn(__fmul_rn(chunk_get(x1, j), r), wa[j]);
+    const float y2 = __fmul_rn(__fmul_rn(chunk_get(x2, j), r), wb[j]);
+    o1[j] = __fsub_rn(__fmul_rn(y1, cs[j]), __fmul_rn(y2, sn[j]));
+    o2[j] = __fadd_rn(__fmul_rn(y2, cs[j]), __fmul_rn(y1, sn[j]));
+  }
+  if (scale) {
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) { o1[j] = __fmul_rn(o1[j], e); o2[j] = __fmul_rn(o2[j], e); }
+  }
+  chunk_set(out1, o1);
+  chunk_set(out2, o2);
+}
+
+// Backward, reduction part of one lane. With g' = g * e (e = exp(scale) for Q,
+// 1 for K) and dn = R^T g' (inverse rotation), it accumulates the d w partials
+// acc += dn * n (n = x * r), keeps dnw = dn * w for the dx part, and returns
+// the lane partial of sum_j dn_j w_j n_j. That sum is also the row's
+// contribution to d scale: <R^T g', n w> = <g', R(n w)> = sum_j dq_out_j q_out_j.
+template <typename T>
+__device__ __forceinline__ float bwd_lane_reduce(const Chunk<T>& x1, const Chunk<T>& x2,
+                                                 const Chunk<T>& g1, const Chunk<T>& g2, float r,
+                                                 float e, bool scale, const float* wa,
+                                                 const float* wb, const float (&sn)[kChunk],
+                                                 const float (&cs)[kChunk],
+                                                 float (&acc1)[kChunk], float (&acc2)[kChunk],
+                                                 float (&dnw1)[kChunk], float (&dnw2)[kChunk]) {
+  float dsum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) {
+    float ga = chunk_get(g1, j), gb = chunk_get(g2, j);
+    if (scale) { ga *= e; gb *= e; }
+    const float d1 = fmaf(ga, cs[j], gb * sn[j]);
+    const float d2 = fmaf(gb, cs[j], -(ga * sn[j]));
+    const float n1 = chunk_get(x1, j) * r, n2 = chunk_get(x2, j) * r;
+    acc1[j] = fmaf(d1, n1, acc1[j]);
+    acc2[j] = fmaf(d2, n2, acc2[j]);
+    dnw1[j] = d1 * wa[j];
+    dnw2[j] = d2 * wb[j];
+    dsum = fmaf(dnw1[j], n1, dsum);
+    dsum = fmaf(dnw2[j], n2, dsum);
+  }
+  return dsum;
+}
+
+// Backward, dx of one lane: dx = r * (dn w - n * m), m = sum(dn w n) / D.
+template <typename T>
+__device__ __forceinline__ void bwd_lane_dx(const Chunk<T>& x1, const Chunk<T>& x2, float r, float m,
+                                            const float (&dnw1)[kChunk], const float (&dnw2)[kChunk],
+                                            Chunk<T>& out1, Chunk<T>& out2) {
+  float o1[kChunk], o2[kChunk];
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) {
+    const float n1 = chunk_get(x1, j) * r, n2 = chunk_get(x2, j) * r;
+    o1[j] = r * fmaf(-n1, m, dnw1[j]);
+    o2[j] = r * fmaf(-n2, m, dnw2[j]);
+  }
+  chunk_set(out1, o1);
+  chunk_set(out2, o2);
+}
+
 // Decompose a CTA thread into (chunk c, head slot hs, position slot ps).
 __device__ __forceinline__ void thread_slots(const Geometry& g, int tid, int& c, int& hs, int& ps) {
   c = tid & ((1 << g.log2_l) - 1);
@@ -198,15 +333,5 @@ __device__ __forceinline__ void thread_slots(const Geometry& g, int tid, int& c,
   }
 }
 
-// item -> (tensor, b, position block, head group); tensor fastest, then positions.
-__device__ __forceinline__ void item_coords(const Geometry& g, int64_t item, int& t, int64_t& b,
-                                            int64_t& pb, int64_t& hg) {
-  t = (int)(item & 1);
-  item >>= 1;
-  pb = item % g.n_pos_blocks;
-  const int64_t rest = item / g.n_pos_blocks;
-  hg = rest % g.n_head_groups;
-  b = rest / g.n_head_groups;
-}
 
 }  // namespace flash_prologue

@@ -28,10 +28,10 @@ __global__ void __launch_bounds__(kThreads) prologue_fwd_kernel(const FwdArgs a)
   const int heads_per_item = a.g.hi * HS;
   const int j0 = c * kChunk;
 
-  for (int64_t item = blockIdx.x; item < a.g.n_items; item += gridDim.x) {
-    int t;
-    int64_t b, pb, hg;
-    item_coords(a.g, item, t, b, pb, hg);
+  Cursor4 cur;
+  for (cur.init(blockIdx.x, a.g.radix); cur.d[3] < a.B; cur.advance(a.g.radix)) {
+    const int t = (int)cur.d[0];
+    const int64_t pb = cur.d[1], hg = cur.d[2], b = cur.d[3];
     const int64_t n = pb * PS + ps;
     const bool pos_ok = n < a.N;
     const T* xb = static_cast<const T*>(a.x[t]);
@@ -60,43 +60,14 @@ __global__ void __launch_bounds__(kThreads) prologue_fwd_kernel(const FwdArgs a)
 #pragma unroll
         for (int k = 0; k < Chunk<T>::kWords; ++k) { x1.w[k] = 0; x2.w[k] = 0; }
       }
-
-      // Sum of the rounded squares, lane-local then across the row's lanes.
-      float ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float u = chunk_get(x1, j);
-        ss = __fadd_rn(ss, __fmul_rn(u, u));
-      }
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float u = chunk_get(x2, j);
-        ss = __fadd_rn(ss, __fmul_rn(u, u));
-      }
-      ss = row_sum<L>(ss);
+      const float ss = row_sum<L>(lane_sumsq(x1, x2));
       if (!ok) continue;  // after the shuffles: every lane took part in them
-
       const float r = inv_rms<D>(ss, a.eps);
-      float o1[kChunk], o2[kChunk];
-      // normed = (x * r) * w; rotate
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float y1 = __fmul_rn(__fmul_rn(chunk_get(x1, j), r), w[j0 + j]);
-        const float y2 = __fmul_rn(__fmul_rn(chunk_get(x2, j), r), w[HALF + j0 + j]);
-        o1[j] = __fsub_rn(__fmul_rn(y1, cs[j]), __fmul_rn(y2, sn[j]));
-        o2[j] = __fadd_rn(__fmul_rn(y2, cs[j]), __fmul_rn(y1, sn[j]));
-      }
-      if (t == 0) {  // Q only: * exp(scale), after the rotation
-        const float e = e_s[h];
-#pragma unroll
-        for (int j = 0; j < kChunk; ++j) { o1[j] = __fmul_rn(o1[j], e); o2[j] = __fmul_rn(o2[j], e); }
-      }
-      Chunk<T> out;
+      Chunk<T> out1, out2;
+      fwd_lane(x1, x2, r, w + j0, w + HALF + j0, sn, cs, t == 0, t == 0 ? e_s[h] : 1.f, out1, out2);
       T* yp = yb + b * sy.b + (int64_t)h * sy.h + n * sy.n + j0;
-      chunk_set(out, o1);
-      store_stream<T, VEC>(yp, out);
-      chunk_set(out, o2);
-      store_stream<T, VEC>(yp + HALF, out);
+      store_stream<T, VEC>(yp, out1);
+      store_stream<T, VEC>(yp + HALF, out2);
     }
   }
 }
@@ -107,7 +78,9 @@ static cudaError_t launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   const void* fn = reinterpret_cast<const void*>(&prologue_fwd_kernel<T, D, VEC>);
   const int64_t grid = persistent_grid(fn, smem, a.g.n_items);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
-  prologue_fwd_kernel<T, D, VEC><<<(unsigned)grid, kThreads, smem, stream>>>(a);
+  FwdArgs args = a;
+  args.g.radix = make_radix(2, a.g.n_pos_blocks, a.g.n_head_groups, grid);
+  prologue_fwd_kernel<T, D, VEC><<<(unsigned)grid, kThreads, smem, stream>>>(args);
   return cudaGetLastError();
 }
 

@@ -56,6 +56,7 @@ struct TmaPlan {
   int stages;
   int64_t inner_ext, outer_ext;
   int64_t n_ib, n_ob, n_tiles;  // tiles = B * n_ob * n_ib, inner block fastest
+  Radix4 radix;                  // digits (inner block, outer block, b); set at launch
 };
 
 // One streamed input: rows along the inner dim are contiguous (stride D).

@@ -38,19 +38,17 @@ struct TmaShape {
 };
 
 struct TileCoords {
-  int64_t b, i0, o0;
-  int vi, vo;
+  int32_t b, i0, o0;  // batch, first inner row, first outer row
+  int vi, vo;         // valid rows along inner / outer
 };
 
-__device__ __forceinline__ TileCoords tile_coords(const TmaPlan& p, int64_t tile) {
+// Tile of a cursor over (inner block, outer block, b); digit 3 flags the end.
+__device__ __forceinline__ TileCoords tile_coords(const TmaPlan& p, const Cursor4& cur) {
   TileCoords tc;
-  const int64_t ib = tile % p.n_ib;
-  const int64_t rest = tile / p.n_ib;
-  const int64_t ob = rest % p.n_ob;
-  tc.b = rest / p.n_ob;
-  tc.i0 = ib * p.ti;
-  tc.o0 = ob * p.to;
-  const int64_t ri = p.inner_ext - tc.i0, ro = p.outer_ext - tc.o0;
+  tc.b = cur.d[2];
+  tc.i0 = cur.d[0] * p.ti;
+  tc.o0 = cur.d[1] * p.to;
+  const int64_t ri = p.inner_ext - (int64_t)tc.i0, ro = p.outer_ext - (int64_t)tc.o0;
   tc.vi = (int)(ri < p.ti ? ri : p.ti);
   tc.vo = (int)(ro < p.to ? ro : p.to);
   return tc;
@@ -74,7 +72,7 @@ __device__ __forceinline__ void issue_stage(const TmaPlan& p, const TmaTensor* i
   // Copy list: per tensor (merged: one copy of vo runs) then two table copies.
   int n_copies = 2;
   for (int t = 0; t < nt; ++t) n_copies += merged[t] ? 1 : copies_per_tensor;
-  const int64_t n_first = p.heads_inner ? tc.o0 : tc.i0;
+  const int64_t n_first = p.heads_inner ? (int64_t)tc.o0 : (int64_t)tc.i0;
   const int np = p.heads_inner ? tc.vo : tc.vi;
   for (int j = lane; j < n_copies; j += 32) {
     int jj = j;
@@ -86,8 +84,8 @@ __device__ __forceinline__ void issue_stage(const TmaPlan& p, const TmaTensor* i
     }
     if (t < nt) {
       const TmaTensor& x = in[t];
-      const int64_t o = tc.o0 + jj;
-      const char* src = x.base + (tc.b * x.sb + o * x.s_outer + tc.i0 * (int64_t)D) * ES;
+      const int64_t o = (int64_t)tc.o0 + jj;
+      const char* src = x.base + ((int64_t)tc.b * x.sb + o * x.s_outer + (int64_t)tc.i0 * D) * ES;
       unsigned char* dst = st + t * kTmaTileBytes + jj * p.ti * ROW_BYTES;
       const uint32_t bytes = merged[t] ? run * (uint32_t)tc.vo : run;
       bulk_g2s(dst, src, bytes, bar, pol_stream);
@@ -95,7 +93,7 @@ __device__ __forceinline__ void issue_stage(const TmaPlan& p, const TmaTensor* i
       const bool is_cos = jj == 1;
       const float* tab = is_cos ? cos : sin;
       const int64_t tb = is_cos ? cos_b : sin_b;
-      const float* src = tab + tc.b * tb + n_first * (D / 2);
+      const float* src = tab + (int64_t)tc.b * tb + n_first * (D / 2);
       unsigned char* dst = st + nt * kTmaTileBytes + (is_cos ? table_bytes : 0);
       bulk_g2s(dst, src, (uint32_t)np * (D / 2) * 4, bar, pol_table);
     }
@@ -119,20 +117,6 @@ __device__ __forceinline__ void lds_chunk(Chunk<T>& c, const unsigned char* p) {
   }
 }
 
-// Same as lds_chunk, but never merged with an earlier read of the same row:
-// the backward re-reads its rows for the dx pass instead of keeping every
-// intermediate of the reduction pass live in registers.
-template <typename T>
-__device__ __forceinline__ void lds_chunk_again(Chunk<T>& c, const unsigned char* p) {
-  const uint32_t a = smem_u32(p);
-#pragma unroll
-  for (int i = 0; i < Chunk<T>::kWords / 4; ++i) {
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(c.w[4 * i + 0]), "=r"(c.w[4 * i + 1]), "=r"(c.w[4 * i + 2]), "=r"(c.w[4 * i + 3])
-                 : "r"(a + 16 * i));
-  }
-}
-
 __device__ __forceinline__ void lds_f8(float (&v)[kChunk], const unsigned char* p) {
   const float4* p4 = reinterpret_cast<const float4*>(p);
   const float4 a = p4[0], b = p4[1];
@@ -145,7 +129,8 @@ __device__ __forceinline__ void lds_f8(float (&v)[kChunk], const unsigned char* 
 // ---------------------------------------------------------------------------
 // Forward
 template <typename T, int D>
-__global__ void __launch_bounds__(kTmaThreads, 2) prologue_fwd_tma_kernel(const __grid_constant__ TmaFwdArgs a) {
+__global__ void __launch_bounds__(kTmaThreads, 2)
+    prologue_fwd_tma_kernel(const __grid_constant__ TmaFwdArgs a) {
   using S_ = TmaShape<T, D>;
   constexpr int HALF = S_::HALF;
   constexpr int L = S_::L;
@@ -171,14 +156,15 @@ __global__ void __launch_bounds__(kTmaThreads, 2) prologue_fwd_tma_kernel(const 
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  Cursor4 cur;
   if (warp == kTmaConsumerWarps) {  // ---------------- producer ----------------
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_table = policy_evict_last();
     int k = 0;
-    for (int64_t tile = blockIdx.x; tile < a.p.n_tiles; tile += gridDim.x, ++k) {
+    for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {
       const int s = k % S;
       if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
-      const TileCoords tc = tile_coords(a.p, tile);
+      const TileCoords tc = tile_coords(a.p, cur);
       unsigned char* st = smem + s * stage_bytes;
       if (lane == 0) mbar_arrive_expect_tx(&full[s], stage_tx_bytes<D, sizeof(T)>(a.p, 2, tc));
       __syncwarp();
@@ -194,18 +180,22 @@ __global__ void __launch_bounds__(kTmaThreads, 2) prologue_fwd_tma_kernel(const 
   const int c = gtid & (L - 1);
   const int slot = gtid >> S_::LOG2_L;
   const int j0 = c * kChunk;
-  const float* w = w_s + t * D;
+  const float* wa = w_s + t * D + j0;
+  const float* wb = wa + HALF;
   T* yb = static_cast<T*>(a.out[t]);
   const RowStrides so = a.so[t];
+  const int64_t so_inner = a.p.heads_inner ? so.h : so.n;
+  const int64_t so_outer = a.p.heads_inner ? so.n : so.h;
   int k = 0;
-  for (int64_t tile = blockIdx.x; tile < a.p.n_tiles; tile += gridDim.x, ++k) {
+  for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {
     const int s = k % S;
     if (!mbar_wait(&full[s], (k / S) & 1)) break;
-    const TileCoords tc = tile_coords(a.p, tile);
+    const TileCoords tc = tile_coords(a.p, cur);
     const unsigned char* st = smem + s * stage_bytes;
     const unsigned char* tile_x = st + t * kTmaTileBytes;
     const unsigned char* sin_s = st + 2 * kTmaTileBytes;
     const unsigned char* cos_s = sin_s + table_bytes;
+    T* ytile = yb + (int64_t)tc.b * so.b + (int64_t)tc.i0 * so_inner + (int64_t)tc.o0 * so_outer + j0;
 #pragma unroll
     for (int pass = 0; pass < S_::PASSES; ++pass) {
       const int r = pass * S_::ROWS_PER_PASS + slot;
@@ -216,45 +206,19 @@ __global__ void __launch_bounds__(kTmaThreads, 2) prologue_fwd_tma_kernel(const 
       Chunk<T> x1, x2;
       lds_chunk(x1, row + j0 * sizeof(T));
       lds_chunk(x2, row + (HALF + j0) * sizeof(T));
-      float ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float u = chunk_get(x1, j);
-        ss = __fadd_rn(ss, __fmul_rn(u, u));
-      }
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float u = chunk_get(x2, j);
-        ss = __fadd_rn(ss, __fmul_rn(u, u));
-      }
-      ss = row_sum<L>(ss);
+      const float ss = row_sum<L>(lane_sumsq(x1, x2));
       if (!ok) continue;
       const float rr = inv_rms<D>(ss, a.eps);
       const int p_l = a.p.heads_inner ? o_l : i_l;
       float sn[kChunk], cs[kChunk];
       lds_f8(sn, sin_s + (p_l * HALF + j0) * 4);
       lds_f8(cs, cos_s + (p_l * HALF + j0) * 4);
-      const int64_t h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
-      const int64_t n = a.p.heads_inner ? tc.o0 + o_l : tc.i0 + i_l;
-      float o1[kChunk], o2[kChunk];
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float y1 = __fmul_rn(__fmul_rn(chunk_get(x1, j), rr), w[j0 + j]);
-        const float y2 = __fmul_rn(__fmul_rn(chunk_get(x2, j), rr), w[HALF + j0 + j]);
-        o1[j] = __fsub_rn(__fmul_rn(y1, cs[j]), __fmul_rn(y2, sn[j]));
-        o2[j] = __fadd_rn(__fmul_rn(y2, cs[j]), __fmul_rn(y1, sn[j]));
-      }
-      if (t == 0) {
-        const float e = e_s[h];
-#pragma unroll
-        for (int j = 0; j < kChunk; ++j) { o1[j] = __fmul_rn(o1[j], e); o2[j] = __fmul_rn(o2[j], e); }
-      }
-      Chunk<T> out;
-      T* yp = yb + tc.b * so.b + h * so.h + n * so.n + j0;
-      chunk_set(out, o1);
-      store_stream<T, true>(yp, out);
-      chunk_set(out, o2);
-      store_stream<T, true>(yp + HALF, out);
+      const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
+      Chunk<T> out1, out2;
+      fwd_lane(x1, x2, rr, wa, wb, sn, cs, t == 0, t == 0 ? e_s[h] : 1.f, out1, out2);
+      T* yp = ytile + (int64_t)i_l * so_inner + (int64_t)o_l * so_outer;
+      store_stream<T, true>(yp, out1);
+      store_stream<T, true>(yp + HALF, out2);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -264,7 +228,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2) prologue_fwd_tma_kernel(const 
 // ---------------------------------------------------------------------------
 // Backward
 template <typename T, int D>
-__global__ void __launch_bounds__(kTmaThreads, 2) prologue_bwd_tma_kernel(const __grid_constant__ TmaBwdArgs a) {
+__global__ void __launch_bounds__(kTmaThreads, 2)
+    prologue_bwd_tma_kernel(const __grid_constant__ TmaBwdArgs a) {
   using S_ = TmaShape<T, D>;
   constexpr int HALF = S_::HALF;
   constexpr int L = S_::L;
@@ -294,14 +259,15 @@ __global__ void __launch_bounds__(kTmaThreads, 2) prologue_bwd_tma_kernel(const 
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  Cursor4 cur;
   if (warp == kTmaConsumerWarps) {  // ---------------- producer ----------------
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_table = policy_evict_last();
     int k = 0;
-    for (int64_t tile = blockIdx.x; tile < a.p.n_tiles; tile += gridDim.x, ++k) {
+    for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {
       const int s = k % S;
       if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
-      const TileCoords tc = tile_coords(a.p, tile);
+      const TileCoords tc = tile_coords(a.p, cur);
       unsigned char* st = smem + s * stage_bytes;
       if (lane == 0) mbar_arrive_expect_tx(&full[s], stage_tx_bytes<D, sizeof(T)>(a.p, 4, tc));
       __syncwarp();
@@ -317,9 +283,12 @@ __global__ void __launch_bounds__(kTmaThreads, 2) prologue_bwd_tma_kernel(const 
   const int c = gtid & (L - 1);
   const int slot = gtid >> LOG2_L;
   const int j0 = c * kChunk;
-  const float* w = w_s + t * D;
+  const float* wa = w_s + t * D + j0;
+  const float* wb = wa + HALF;
   T* db = static_cast<T*>(a.dx[t]);
   const RowStrides sd = a.sd[t];
+  const int64_t sd_inner = a.p.heads_inner ? sd.h : sd.n;
+  const int64_t sd_outer = a.p.heads_inner ? sd.n : sd.h;
 
   // Lanes (within a warp) that hold rows of the same head differ only in the
   // chunk bits and in the lane bits [ps_lo, ps_hi).
@@ -339,15 +308,16 @@ __global__ void __launch_bounds__(kTmaThreads, 2) prologue_bwd_tma_kernel(const 
   for (int j = 0; j < kChunk; ++j) { acc1[j] = 0.f; acc2[j] = 0.f; }
 
   int k = 0;
-  for (int64_t tile = blockIdx.x; tile < a.p.n_tiles; tile += gridDim.x, ++k) {
+  for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {
     const int s = k % S;
     if (!mbar_wait(&full[s], (k / S) & 1)) break;
-    const TileCoords tc = tile_coords(a.p, tile);
+    const TileCoords tc = tile_coords(a.p, cur);
     const unsigned char* st = smem + s * stage_bytes;
     const unsigned char* tile_x = st + (2 * t) * kTmaTileBytes;
     const unsigned char* tile_g = st + (2 * t + 1) * kTmaTileBytes;
     const unsigned char* sin_s = st + 4 * kTmaTileBytes;
     const unsigned char* cos_s = sin_s + table_bytes;
+    T* dtile = db + (int64_t)tc.b * sd.b + (int64_t)tc.i0 * sd_inner + (int64_t)tc.o0 * sd_outer + j0;
 #pragma unroll 1
     for (int pass = 0; pass < S_::PASSES; ++pass) {
       const int r = pass * S_::ROWS_PER_PASS + slot;
@@ -355,6 +325,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2) prologue_bwd_tma_kernel(const 
       const int i_l = r & (a.p.ti - 1);
       const bool ok = o_l < tc.vo && i_l < tc.vi;
       Chunk<T> x1, x2, g1, g2;
+      float sn[kChunk], cs[kChunk];
       if (ok) {
         const unsigned char* xr = tile_x + r * S_::ROW_BYTES;
         const unsigned char* gr = tile_g + r * S_::ROW_BYTES;
@@ -362,87 +333,33 @@ __global__ void __launch_bounds__(kTmaThreads, 2) prologue_bwd_tma_kernel(const 
         lds_chunk(x2, xr + (HALF + j0) * sizeof(T));
         lds_chunk(g1, gr + j0 * sizeof(T));
         lds_chunk(g2, gr + (HALF + j0) * sizeof(T));
-      } else {
-#pragma unroll
-        for (int q = 0; q < Chunk<T>::kWords; ++q) { x1.w[q] = 0; x2.w[q] = 0; g1.w[q] = 0; g2.w[q] = 0; }
-      }
-      const int p_l = a.p.heads_inner ? o_l : i_l;
-      float sn[kChunk], cs[kChunk];
-      if (ok) {
+        const int p_l = a.p.heads_inner ? o_l : i_l;
         lds_f8(sn, sin_s + (p_l * HALF + j0) * 4);
         lds_f8(cs, cos_s + (p_l * HALF + j0) * 4);
       } else {
 #pragma unroll
+        for (int q = 0; q < Chunk<T>::kWords; ++q) { x1.w[q] = 0; x2.w[q] = 0; g1.w[q] = 0; g2.w[q] = 0; }
+#pragma unroll
         for (int j = 0; j < kChunk; ++j) { sn[j] = 0.f; cs[j] = 0.f; }
       }
-      const int64_t h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
-      const int64_t n = a.p.heads_inner ? tc.o0 + o_l : tc.i0 + i_l;
+      const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
-
-      float ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        float v = chunk_get(x1, j); ss = __fadd_rn(ss, __fmul_rn(v, v));
-      }
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        float v = chunk_get(x2, j); ss = __fadd_rn(ss, __fmul_rn(v, v));
-      }
-      ss = row_sum<L>(ss);
-      const float rr = inv_rms<D>(ss, a.eps);
-
-      // Pass 1: reductions (d w partials, sum(dn w n), d scales).
-      float dsum = 0.f, ds_part = 0.f;
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float n1 = chunk_get(x1, j) * rr, n2 = chunk_get(x2, j) * rr;
-        const float gg1 = chunk_get(g1, j) * e, gg2 = chunk_get(g2, j) * e;
-        const float d1 = gg1 * cs[j] + gg2 * sn[j];
-        const float d2 = gg2 * cs[j] - gg1 * sn[j];
-        const float wa = w[j0 + j], wb = w[HALF + j0 + j];
-        if (t == 0) {
-          const float ya = n1 * wa, yb = n2 * wb;
-          ds_part += gg1 * (ya * cs[j] - yb * sn[j]) + gg2 * (yb * cs[j] + ya * sn[j]);
-        }
-        acc1[j] += d1 * n1;
-        acc2[j] += d2 * n2;
-        dsum += d1 * wa * n1 + d2 * wb * n2;
-      }
-      dsum = row_sum<L>(dsum);
+      const float rr = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
+      float dnw1[kChunk], dnw2[kChunk];
+      const float dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, rr, e, t == 0, wa, wb, sn, cs,
+                                                    acc1, acc2, dnw1, dnw2));
       if (t == 0) {
-        ds_part = row_sum<L>(ds_part);
+        float v = dsum;
         for (int bit = ps_lo; bit < ps_hi; ++bit)
-          ds_part = __fadd_rn(ds_part, __shfl_xor_sync(0xffffffffu, ds_part, 1 << bit));
-        if (ds_writer && h < a.H) ds_s[warp * a.H + h] += ds_part;
+          v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1 << bit));
+        if (ds_writer && h < a.H) ds_s[warp * a.H + h] += v;
       }
       if (!ok) continue;
-      // Pass 2: dx = r (dn w - n mean(dn w n)), with dn recomputed from the
-      // rows re-read from shared memory (same expressions as pass 1).
-      const float m = dsum * (1.0f / (float)D);
-      {
-        const unsigned char* xr = tile_x + r * S_::ROW_BYTES;
-        const unsigned char* gr = tile_g + r * S_::ROW_BYTES;
-        lds_chunk_again(x1, xr + j0 * sizeof(T));
-        lds_chunk_again(x2, xr + (HALF + j0) * sizeof(T));
-        lds_chunk_again(g1, gr + j0 * sizeof(T));
-        lds_chunk_again(g2, gr + (HALF + j0) * sizeof(T));
-      }
-      float o1[kChunk], o2[kChunk];
-#pragma unroll
-      for (int j = 0; j < kChunk; ++j) {
-        const float n1 = chunk_get(x1, j) * rr, n2 = chunk_get(x2, j) * rr;
-        const float gg1 = chunk_get(g1, j) * e, gg2 = chunk_get(g2, j) * e;
-        const float d1 = gg1 * cs[j] + gg2 * sn[j];
-        const float d2 = gg2 * cs[j] - gg1 * sn[j];
-        o1[j] = rr * (d1 * w[j0 + j] - n1 * m);
-        o2[j] = rr * (d2 * w[HALF + j0 + j] - n2 * m);
-      }
-      Chunk<T> out;
-      T* dp = db + tc.b * sd.b + h * sd.h + n * sd.n + j0;
-      chunk_set(out, o1);
-      store_stream<T, true>(dp, out);
-      chunk_set(out, o2);
-      store_stream<T, true>(dp + HALF, out);
+      Chunk<T> out1, out2;
+      bwd_lane_dx(x1, x2, rr, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
+      T* dp = dtile + (int64_t)i_l * sd_inner + (int64_t)o_l * sd_outer;
+      store_stream<T, true>(dp, out1);
+      store_stream<T, true>(dp + HALF, out2);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -546,7 +463,9 @@ cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t s
   if (err != cudaSuccess) return err;
   const int64_t grid = persistent_grid(fn, smem, a.p.n_tiles, kTmaThreads);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
-  void* args[] = {const_cast<TmaFwdArgs*>(&a)};
+  TmaFwdArgs launch_args = a;
+  launch_args.p.radix = make_radix(a.p.n_ib, a.p.n_ob, a.B, grid);
+  void* args[] = {&launch_args};
   return cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kTmaThreads), args, smem, stream);
 }
 
@@ -559,7 +478,9 @@ cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype,
   if (err != cudaSuccess) return err;
   const int64_t grid = persistent_grid(fn, smem, a.p.n_tiles, kTmaThreads);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
-  void* args[] = {const_cast<TmaBwdArgs*>(&a)};
+  TmaBwdArgs launch_args = a;
+  launch_args.p.radix = make_radix(a.p.n_ib, a.p.n_ob, a.B, grid);
+  void* args[] = {&launch_args};
   err = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kTmaThreads), args, smem, stream);
   if (err != cudaSuccess) return err;
   return launch_bwd_finalize(a.partials, grid, 2 * D + a.H, 2 * D, dw, ds, stream);
