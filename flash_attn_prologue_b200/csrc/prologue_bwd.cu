@@ -67,9 +67,9 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
   }
   const bool ds_writer = (lane & ((1 << ps_hi) - 1) & ~((1 << ps_lo) - 1)) == 0 && c == 0;
 
-  float acc1[kChunk], acc2[kChunk];  // d w partials for elements j0.. and HALF+j0..
+  float2 acc1p[kPairs], acc2p[kPairs];  // d w partials for elements j0.. and HALF+j0..
 #pragma unroll
-  for (int j = 0; j < kChunk; ++j) { acc1[j] = 0.f; acc2[j] = 0.f; }
+  for (int q = 0; q < kPairs; ++q) { acc1p[q] = make_float2(0.f, 0.f); acc2p[q] = make_float2(0.f, 0.f); }
 
   Cursor4 cur;
   for (cur.init(blockIdx.x, a.g.radix); cur.d[3] < a.B; cur.advance(a.g.radix)) {
@@ -103,9 +103,9 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
       }
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
       const float r = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
-      float dnw1[kChunk], dnw2[kChunk];
+      float2 dnw1[kPairs], dnw2[kPairs];
       const float dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, r, e, t == 0, w + j0,
-                                                    w + HALF + j0, sn, cs, acc1, acc2, dnw1, dnw2));
+                                                    w + HALF + j0, sn, cs, acc1p, acc2p, dnw1, dnw2));
       if (t == 0) {
         // d scales: the row's sum(dn w n), reduced over the warp's position slots.
         float v = dsum;
@@ -123,6 +123,9 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
   }
 
   // d w: combine lanes that hold the same chunk (fixed xor order), then warps.
+  float acc1[kChunk], acc2[kChunk];
+  unpair(acc1p, acc1);
+  unpair(acc2p, acc2);
 #pragma unroll
   for (int j = 0; j < kChunk; ++j) {
 #pragma unroll

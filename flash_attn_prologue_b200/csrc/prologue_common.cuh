@@ -230,47 +230,88 @@ __device__ __forceinline__ float inv_rms(float sumsq, float eps) {
 // ---------------------------------------------------------------------------
 // Per-row arithmetic shared by the register-path and the bulk-copy kernels (so
 // both give bit-identical results). A lane holds the chunk pair
-// x1 = x[j0 .. j0+8), x2 = x[D/2+j0 .. D/2+j0+8) of its row.
+// x1 = x[j0 .. j0+8), x2 = x[D/2+j0 .. D/2+j0+8) of its row and works on
+// element pairs (2p, 2p+1) with sm_100's paired FP32 instructions
+// (__fmul2_rn / __fadd2_rn / __ffma2_rn): each half rounds exactly like the
+// scalar IEEE operation, at half the instruction count.
+constexpr int kPairs = kChunk / 2;
 
-// Lane-partial sum of squares. For 16-bit inputs x*x is exact in FP32, so the
-// fused multiply-add rounds exactly like "square, then add".
+template <typename T>
+__device__ __forceinline__ float2 chunk_get2(const Chunk<T>& c, int p);
+
+template <>
+__device__ __forceinline__ float2 chunk_get2<__nv_bfloat16>(const Chunk<__nv_bfloat16>& c, int p) {
+  const uint32_t word = c.w[p];
+  return make_float2(__uint_as_float(word << 16), __uint_as_float(word & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float2 chunk_get2<__half>(const Chunk<__half>& c, int p) {
+  const uint32_t word = c.w[p];
+  return __half22float2(*reinterpret_cast<const __half2*>(&word));
+}
+template <>
+__device__ __forceinline__ float2 chunk_get2<float>(const Chunk<float>& c, int p) {
+  return make_float2(__uint_as_float(c.w[2 * p]), __uint_as_float(c.w[2 * p + 1]));
+}
+
+template <typename T>
+__device__ __forceinline__ void chunk_set2(Chunk<T>& c, const float2 (&v)[kPairs]) {
+  float f[kChunk];
+#pragma unroll
+  for (int p = 0; p < kPairs; ++p) { f[2 * p] = v[p].x; f[2 * p + 1] = v[p].y; }
+  chunk_set(c, f);
+}
+
+__device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 neg2(float2 v) { return make_float2(-v.x, -v.y); }
+__device__ __forceinline__ float2 ld_pair(const float* p, int q) {
+  return reinterpret_cast<const float2*>(p)[q];
+}
+
+// Lane-partial sum of squares over two interleaved pair accumulators. For
+// 16-bit inputs x*x is exact in FP32, so the fused multiply-add rounds exactly
+// like "square, then add"; FP32 inputs square and add separately.
 template <typename T>
 __device__ __forceinline__ float lane_sumsq(const Chunk<T>& x1, const Chunk<T>& x2) {
-  float ss = 0.f;
+  float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int j = 0; j < kChunk; ++j) {
-    const float u = chunk_get(x1, j);
-    ss = (sizeof(T) == 2) ? fmaf(u, u, ss) : __fadd_rn(ss, __fmul_rn(u, u));
+  for (int p = 0; p < kPairs; ++p) {
+    const float2 u = chunk_get2(x1, p);
+    acc = (sizeof(T) == 2) ? __ffma2_rn(u, u, acc) : __fadd2_rn(acc, __fmul2_rn(u, u));
   }
 #pragma unroll
-  for (int j = 0; j < kChunk; ++j) {
-    const float u = chunk_get(x2, j);
-    ss = (sizeof(T) == 2) ? fmaf(u, u, ss) : __fadd_rn(ss, __fmul_rn(u, u));
+  for (int p = 0; p < kPairs; ++p) {
+    const float2 u = chunk_get2(x2, p);
+    acc = (sizeof(T) == 2) ? __ffma2_rn(u, u, acc) : __fadd2_rn(acc, __fmul2_rn(u, u));
   }
-  return ss;
+  return __fadd_rn(acc.x, acc.y);
 }
 
 // Forward outputs of one lane: normed = (x * r) * w, rotated, times e for Q.
-// Every product and sum rounds separately, as in the eager formulation.
+// Every product and sum rounds separately, as in the eager formulation
+// (a - b is computed as a + (-b), which rounds identically).
 template <typename T>
 __device__ __forceinline__ void fwd_lane(const Chunk<T>& x1, const Chunk<T>& x2, float r,
                                          const float* wa, const float* wb, const float (&sn)[kChunk],
                                          const float (&cs)[kChunk], bool scale, float e,
                                          Chunk<T>& out1, Chunk<T>& out2) {
-  float o1[kChunk], o2[kChunk];
+  const float2 r2 = splat2(r), e2 = splat2(e);
+  float2 o1[kPairs], o2[kPairs];
 #pragma unroll
-  for (int j = 0; j < kChunk; ++j) {
-    const float y1 = __fmul_rn(__fmul_rn(chunk_get(x1, j), r), wa[j]);
-    const float y2 = __fmul_rn(__fmul_rn(chunk_get(x2, j), r), wb[j]);
-    o1[j] = __fsub_rn(__fmul_rn(y1, cs[j]), __fmul_rn(y2, sn[j]));
-    o2[j] = __fadd_rn(__fmul_rn(y2, cs[j]), __fmul_rn(y1, sn[j]));
+  for (int p = 0; p < kPairs; ++p) {
+    const float2 c2 = make_float2(cs[2 * p], cs[2 * p + 1]);
+    const float2 s2 = make_float2(sn[2 * p], sn[2 * p + 1]);
+    const float2 y1 = __fmul2_rn(__fmul2_rn(chunk_get2(x1, p), r2), ld_pair(wa, p));
+    const float2 y2 = __fmul2_rn(__fmul2_rn(chunk_get2(x2, p), r2), ld_pair(wb, p));
+    o1[p] = __fadd2_rn(__fmul2_rn(y1, c2), neg2(__fmul2_rn(y2, s2)));
+    o2[p] = __fadd2_rn(__fmul2_rn(y2, c2), __fmul2_rn(y1, s2));
+    if (scale) {
+      o1[p] = __fmul2_rn(o1[p], e2);
+      o2[p] = __fmul2_rn(o2[p], e2);
+    }
   }
-  if (scale) {
-#pragma unroll
-    for (int j = 0; j < kChunk; ++j) { o1[j] = __fmul_rn(o1[j], e); o2[j] = __fmul_rn(o2[j], e); }
-  }
-  chunk_set(out1, o1);
-  chunk_set(out2, o2);
+  chunk_set2(out1, o1);
+  chunk_set2(out2, o2);
 }
 
 // Backward, reduction part of one lane. With g' = g * e (e = exp(scale) for Q,
@@ -284,40 +325,52 @@ __device__ __forceinline__ float bwd_lane_reduce(const Chunk<T>& x1, const Chunk
                                                  float e, bool scale, const float* wa,
                                                  const float* wb, const float (&sn)[kChunk],
                                                  const float (&cs)[kChunk],
-                                                 float (&acc1)[kChunk], float (&acc2)[kChunk],
-                                                 float (&dnw1)[kChunk], float (&dnw2)[kChunk]) {
-  float dsum = 0.f;
+                                                 float2 (&acc1)[kPairs], float2 (&acc2)[kPairs],
+                                                 float2 (&dnw1)[kPairs], float2 (&dnw2)[kPairs]) {
+  const float2 r2 = splat2(r), e2 = splat2(e);
+  float2 dsum = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int j = 0; j < kChunk; ++j) {
-    float ga = chunk_get(g1, j), gb = chunk_get(g2, j);
-    if (scale) { ga *= e; gb *= e; }
-    const float d1 = fmaf(ga, cs[j], gb * sn[j]);
-    const float d2 = fmaf(gb, cs[j], -(ga * sn[j]));
-    const float n1 = chunk_get(x1, j) * r, n2 = chunk_get(x2, j) * r;
-    acc1[j] = fmaf(d1, n1, acc1[j]);
-    acc2[j] = fmaf(d2, n2, acc2[j]);
-    dnw1[j] = d1 * wa[j];
-    dnw2[j] = d2 * wb[j];
-    dsum = fmaf(dnw1[j], n1, dsum);
-    dsum = fmaf(dnw2[j], n2, dsum);
+  for (int p = 0; p < kPairs; ++p) {
+    const float2 c2 = make_float2(cs[2 * p], cs[2 * p + 1]);
+    const float2 s2 = make_float2(sn[2 * p], sn[2 * p + 1]);
+    float2 ga = chunk_get2(g1, p), gb = chunk_get2(g2, p);
+    if (scale) { ga = __fmul2_rn(ga, e2); gb = __fmul2_rn(gb, e2); }
+    const float2 d1 = __ffma2_rn(ga, c2, __fmul2_rn(gb, s2));
+    const float2 d2 = __ffma2_rn(gb, c2, neg2(__fmul2_rn(ga, s2)));
+    const float2 n1 = __fmul2_rn(chunk_get2(x1, p), r2);
+    const float2 n2 = __fmul2_rn(chunk_get2(x2, p), r2);
+    acc1[p] = __ffma2_rn(d1, n1, acc1[p]);
+    acc2[p] = __ffma2_rn(d2, n2, acc2[p]);
+    dnw1[p] = __fmul2_rn(d1, ld_pair(wa, p));
+    dnw2[p] = __fmul2_rn(d2, ld_pair(wb, p));
+    dsum = __ffma2_rn(dnw1[p], n1, dsum);
+    dsum = __ffma2_rn(dnw2[p], n2, dsum);
   }
-  return dsum;
+  return __fadd_rn(dsum.x, dsum.y);
 }
 
 // Backward, dx of one lane: dx = r * (dn w - n * m), m = sum(dn w n) / D.
 template <typename T>
 __device__ __forceinline__ void bwd_lane_dx(const Chunk<T>& x1, const Chunk<T>& x2, float r, float m,
-                                            const float (&dnw1)[kChunk], const float (&dnw2)[kChunk],
+                                            const float2 (&dnw1)[kPairs], const float2 (&dnw2)[kPairs],
                                             Chunk<T>& out1, Chunk<T>& out2) {
-  float o1[kChunk], o2[kChunk];
+  const float2 r2 = splat2(r), nm2 = splat2(-m);
+  float2 o1[kPairs], o2[kPairs];
 #pragma unroll
-  for (int j = 0; j < kChunk; ++j) {
-    const float n1 = chunk_get(x1, j) * r, n2 = chunk_get(x2, j) * r;
-    o1[j] = r * fmaf(-n1, m, dnw1[j]);
-    o2[j] = r * fmaf(-n2, m, dnw2[j]);
+  for (int p = 0; p < kPairs; ++p) {
+    const float2 n1 = __fmul2_rn(chunk_get2(x1, p), r2);
+    const float2 n2 = __fmul2_rn(chunk_get2(x2, p), r2);
+    o1[p] = __fmul2_rn(r2, __ffma2_rn(n1, nm2, dnw1[p]));
+    o2[p] = __fmul2_rn(r2, __ffma2_rn(n2, nm2, dnw2[p]));
   }
-  chunk_set(out1, o1);
-  chunk_set(out2, o2);
+  chunk_set2(out1, o1);
+  chunk_set2(out2, o2);
+}
+
+// Sum of a lane's two d w pair accumulators into 8 element values.
+__device__ __forceinline__ void unpair(const float2 (&a)[kPairs], float (&v)[kChunk]) {
+#pragma unroll
+  for (int p = 0; p < kPairs; ++p) { v[2 * p] = a[p].x; v[2 * p + 1] = a[p].y; }
 }
 
 // Decompose a CTA thread into (chunk c, head slot hs, position slot ps).

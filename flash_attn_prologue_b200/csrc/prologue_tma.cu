@@ -303,9 +303,9 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   }
   const bool ds_writer = ((lane & ((1 << ps_hi) - 1)) >> ps_lo) == 0 && c == 0;
 
-  float acc1[kChunk], acc2[kChunk];
+  float2 acc1p[kPairs], acc2p[kPairs];  // d w partials for elements j0.. and HALF+j0..
 #pragma unroll
-  for (int j = 0; j < kChunk; ++j) { acc1[j] = 0.f; acc2[j] = 0.f; }
+  for (int q = 0; q < kPairs; ++q) { acc1p[q] = make_float2(0.f, 0.f); acc2p[q] = make_float2(0.f, 0.f); }
 
   int k = 0;
   for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {
@@ -345,9 +345,9 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
       const float rr = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
-      float dnw1[kChunk], dnw2[kChunk];
+      float2 dnw1[kPairs], dnw2[kPairs];
       const float dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, rr, e, t == 0, wa, wb, sn, cs,
-                                                    acc1, acc2, dnw1, dnw2));
+                                                    acc1p, acc2p, dnw1, dnw2));
       if (t == 0) {
         float v = dsum;
         for (int bit = ps_lo; bit < ps_hi; ++bit)
@@ -366,6 +366,9 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   }
 
   // d w: combine lanes holding the same chunk (fixed xor order), then warps.
+  float acc1[kChunk], acc2[kChunk];
+  unpair(acc1p, acc1);
+  unpair(acc2p, acc2);
 #pragma unroll
   for (int j = 0; j < kChunk; ++j) {
 #pragma unroll
