@@ -44,9 +44,12 @@ T_TOKENS, HEADS, HEAD_DIM = 1 << 20, 16, 64
 THETA, RESET = 10000.0, 4096
 FWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 4 + HEAD_DIM * 4
 BWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 6 + HEAD_DIM * 4
-# DRAM traffic per launch from one ncu capture (dram__bytes_read.sum +
-# dram__bytes_write.sum) at a reduced T, scaled by tokens; None until captured.
-NCU_TRAFFIC_BYTES_PER_TOKEN = {"fwd": None, "bwd": None}
+# DRAM traffic per token, dram__bytes_read.sum + dram__bytes_write.sum of one
+# ncu capture of each kernel at T = 131,072 (profiles/prologue_tma_c2_t131072.md),
+# scaled to a launch by the tokens it processes. Writes still dirty in L2 when a
+# kernel ends are not counted by the capture, so traffic reads slightly below
+# the algorithmic bytes.
+NCU_TRAFFIC_BYTES_PER_TOKEN = {"fwd": 8012, "bwd": 12136}
 
 
 def measured_peak():
@@ -72,7 +75,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -287,7 +290,7 @@ def run_ours(args, world, rank, local):
         "bwd": {"ms": round(bwd_ms, 4), "gbs": round(bwd_gbs, 1),
                 "frac_of_measured": round(bwd_gbs / peak, 4),
                 "pct_of_8tbs": round(100 * bwd_gbs / NOMINAL_HBM_GBS, 2)},
-        "roofline": {"kernel": "prologue_bwd_kernel (+ finalize)", "bound": "hbm",
+        "roofline": {"kernel": "prologue_bwd_tma_kernel (+ finalize)", "bound": "hbm",
                      "achieved": round(bwd_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(bwd_gbs / peak, 4), "peak_source": peak_kind,
                      "traffic": (round(traffic * T) if traffic else None)},
@@ -360,8 +363,8 @@ def run_e2e(args, T, device, w, s, world):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=T_TOKENS, help="tokens per GPU (default: C2)")
     ap.add_argument("--e2e-tokens", type=int, default=T_TOKENS // 4)

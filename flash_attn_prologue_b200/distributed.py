@@ -35,8 +35,9 @@ def reduce_param_grads(dw: torch.Tensor, ds: torch.Tensor, group: Optional[dist.
     if world == 1:
         return unpack_param_grads(flat, dw, ds)
     if deterministic:
-        gathered = torch.empty((world, flat.numel()), dtype=flat.dtype, device=flat.device)
+        gathered = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
         dist.all_gather_into_tensor(gathered, flat, group=group)
+        gathered = gathered.view(world, flat.numel())
         total = gathered[0].clone()
         for r in range(1, world):  # fixed rank order
             total += gathered[r]
