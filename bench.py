@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload ("C2"): packed forward + backward of
+Workload (benchmark configuration C2): packed forward + backward of
 qknorm_rope_scale on q/k that are strided views of one BF16 QKV buffer
 [T=1,048,576, 3, H=16, D=64], sin/cos FP32 [T, 32] (theta 10000, positions
 restart every 4096 tokens), scales ~N(0, 0.1), upstream gradients ~N(0, 1).
@@ -45,7 +45,7 @@ THETA, RESET = 10000.0, 4096
 FWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 4 + HEAD_DIM * 4
 BWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 6 + HEAD_DIM * 4
 # DRAM traffic per token, dram__bytes_read.sum + dram__bytes_write.sum of one
-# ncu capture of each kernel at T = 131,072 (profiles/prologue_tma_c2_t131072.md),
+# ncu capture of each kernel at T = 131,072 (summary kept under profiles/),
 # scaled to a launch by the tokens it processes. Writes still dirty in L2 when a
 # kernel ends are not counted by the capture, so traffic reads slightly below
 # the algorithmic bytes.
