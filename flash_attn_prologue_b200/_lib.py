@@ -23,6 +23,7 @@ ERR_EXPANDED = 4
 ERR_WORKSPACE = 5
 ERR_CUDA = 6
 ERR_ALIGNMENT = 7
+ERR_SCRATCH_LIMIT = 8
 
 DTYPE_CODES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 
@@ -38,6 +39,10 @@ SIGNATURES = {
                             ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
     "flash_prologue_bwd_workspace_size": ([_i64, _i64, _i64, _i64, ctypes.c_int,
                                            ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "flash_prologue_bwd_noalloc": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,
+                                    _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
+                                    _i64, _i64, _i64, _i64, ctypes.c_float, ctypes.c_int, _vp],
+                                   ctypes.c_int),
     "flash_prologue_set_path": ([ctypes.c_int], ctypes.c_int),
     "flash_prologue_device_error": ([ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
     "flash_prologue_bwd": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,

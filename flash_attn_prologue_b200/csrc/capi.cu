@@ -247,6 +247,9 @@ const char* flash_prologue_status_string(int status) {
     case FLASH_PROLOGUE_ERR_WORKSPACE: return "workspace missing or too small";
     case FLASH_PROLOGUE_ERR_CUDA: return "CUDA launch or runtime error";
     case FLASH_PROLOGUE_ERR_ALIGNMENT: return "pointer alignment not supported";
+    case FLASH_PROLOGUE_ERR_SCRATCH_LIMIT:
+      return "problem needs more than the 1 MiB static scratch of flash_prologue_bwd_noalloc; "
+             "use flash_prologue_bwd with a workspace";
     default: return "unknown status";
   }
 }

@@ -53,7 +53,8 @@ enum flash_prologue_status {
   FLASH_PROLOGUE_ERR_EXPANDED = 4,         /* stride 0 on a dim of size > 1    */
   FLASH_PROLOGUE_ERR_WORKSPACE = 5,        /* workspace missing or too small   */
   FLASH_PROLOGUE_ERR_CUDA = 6,             /* launch or runtime error          */
-  FLASH_PROLOGUE_ERR_ALIGNMENT = 7         /* pointer alignment the path needs */
+  FLASH_PROLOGUE_ERR_ALIGNMENT = 7,        /* pointer alignment the path needs */
+  FLASH_PROLOGUE_ERR_SCRATCH_LIMIT = 8     /* problem too large for the static scratch */
 };
 
 enum flash_prologue_dtype {
@@ -123,6 +124,35 @@ FLASH_PROLOGUE_API int flash_prologue_bwd(const void* q, const int64_t q_strides
                        void* grad_k, const int64_t dk_strides[4],
                        float* grad_rmsnorm_weight, float* grad_scales,
                        void* workspace, size_t workspace_bytes,
+                       int64_t B, int64_t H, int64_t N, int64_t D,
+                       float eps, int dtype, void* stream);
+
+/*
+ * Backward prologue that allocates nothing: the same computation and results
+ * as flash_prologue_bwd, without the `workspace` arguments. For callers that
+ * cannot allocate device memory per call (runtimes that plan all device memory
+ * up front, host-language bindings without a device allocator, code running
+ * while another framework's pool holds the device heap). Its scratch is a
+ * static 1 MiB array in the library's device memory, held by every GPU that
+ * loads the library until exit. The first call on a device looks up that
+ * array's address with the device current: make it before any stream capture.
+ * All calls on a device share the array, so calls that overlap on the GPU race
+ * and must be serialised; nothing in it needs clearing between calls.
+ * Problems that need more than 1 MiB of scratch (see
+ * flash_prologue_bwd_workspace_size) return FLASH_PROLOGUE_ERR_SCRATCH_LIMIT.
+ * No counterpart in the reference, whose backward allocates its outputs and
+ * zeroed accumulators through PyTorch (fused_epilogue.py:1399-1404).
+ */
+FLASH_PROLOGUE_API int flash_prologue_bwd_noalloc(const void* q, const int64_t q_strides[4],
+                       const void* k, const int64_t k_strides[4],
+                       const float* rmsnorm_weight, const float* scales,
+                       const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3],
+                       const void* grad_q_out, const int64_t gq_strides[4],
+                       const void* grad_k_out, const int64_t gk_strides[4],
+                       void* grad_q, const int64_t dq_strides[4],
+                       void* grad_k, const int64_t dk_strides[4],
+                       float* grad_rmsnorm_weight, float* grad_scales,
                        int64_t B, int64_t H, int64_t N, int64_t D,
                        float eps, int dtype, void* stream);
 
