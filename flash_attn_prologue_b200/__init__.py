@@ -16,6 +16,8 @@ __version__ = "0.2.0"
 _LAZY = {
     "qknorm_rope_scale_cute_op": ("fused_epilogue", "qknorm_rope_scale_cute_op"),
     "qknorm_rope_scale_cute_backward_op": ("fused_epilogue", "qknorm_rope_scale_cute_backward_op"),
+    "fused_qkv": ("fused_qkv", "fused_qkv_op"),
+    "fused_qkv_epilogue": ("fused_qkv", "fused_qkv_epilogue_op"),
 }
 __all__ = ["qknorm_rope_scale", "prepare_backend", "RMSNormRoPEScale", *_LAZY]
 
@@ -25,6 +27,9 @@ def __getattr__(name):
         raise AttributeError(name)
     module, symbol = _LAZY[name]
     loaded = import_module(f".{module}", __name__)
-    value = getattr(loaded, symbol)
-    globals()[name] = value
-    return value
+    # Importing the submodule binds the package attribute of the same name to
+    # the module; restore every public alias that it provides.
+    for alias, (source, exported) in _LAZY.items():
+        if source == module:
+            globals()[alias] = getattr(loaded, exported)
+    return globals()[name]

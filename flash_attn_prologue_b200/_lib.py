@@ -43,6 +43,9 @@ SIGNATURES = {
                                     _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
                                     _i64, _i64, _i64, _i64, ctypes.c_float, ctypes.c_int, _vp],
                                    ctypes.c_int),
+    "flash_prologue_qkv_gemm_fwd": ([_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp,
+                                     _vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _vp, _vp,
+                                     ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
     "flash_prologue_set_path": ([ctypes.c_int], ctypes.c_int),
     "flash_prologue_device_error": ([ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
     "flash_prologue_bwd": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,

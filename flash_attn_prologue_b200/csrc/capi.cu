@@ -227,8 +227,12 @@ extern "C" {
 
 FLASH_PROLOGUE_API int flash_prologue_device_error(int* value, int reset) {
   if (!value) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
-  return read_device_error(value, reset != 0) == cudaSuccess ? FLASH_PROLOGUE_OK
-                                                             : FLASH_PROLOGUE_ERR_CUDA;
+  int a = 0, b = 0;
+  if (read_device_error(&a, reset != 0) != cudaSuccess ||
+      read_gemm_device_error(&b, reset != 0) != cudaSuccess)
+    return FLASH_PROLOGUE_ERR_CUDA;
+  *value = a | b;
+  return FLASH_PROLOGUE_OK;
 }
 
 FLASH_PROLOGUE_API int flash_prologue_set_path(int mode) {

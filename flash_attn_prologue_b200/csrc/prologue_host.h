@@ -98,8 +98,10 @@ struct TmaBwdArgs {
 
 TmaPlan plan_tma(int64_t B, int64_t H, int64_t N, int D, int dtype, bool heads_inner, int stages);
 size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H);
-// Reads (synchronously) and optionally clears the bulk-copy kernels' error word.
+// Read (synchronously) and optionally clear the error words of the bulk-copy
+// prologue kernels and of the fused QKV GEMM.
 cudaError_t read_device_error(int* value, bool reset);
+cudaError_t read_gemm_device_error(int* value, bool reset);
 int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype);
 cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream);
 cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype, int D,

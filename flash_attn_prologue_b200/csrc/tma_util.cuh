@@ -15,9 +15,9 @@ constexpr int kDeviceErrorTimeout = 1;
 constexpr uint32_t kMaxWaitTries = 1u << 22;  // x suspend hint below: about 4 s
 constexpr uint32_t kSuspendHintNs = 1000;
 
-// Device error word of the bulk-copy kernels (0 = no error). One definition
-// per translation unit that includes this header (the library is built
-// without relocatable device code); only prologue_tma.cu includes it.
+// Device error word of the waits in this translation unit (0 = no error). The
+// library is built without relocatable device code, so every .cu file that
+// includes this header has its own word and its own host-side reader.
 static __device__ int g_device_error = 0;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

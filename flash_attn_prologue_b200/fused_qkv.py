@@ -1,0 +1,185 @@
+"""Fused QKV projection with the prologue in the GEMM epilogue (tcgen05/TMEM, sm_100a).
+
+Custom ops under the reference's names (flash_attn_prologue/fused_qkv.py):
+
+* ``flash_prologue::fused_qkv(x, weight) -> (q, k, v)``: the projection
+  ``x @ weight.T`` split into per-head ``[B, H, N, D]`` BF16 tensors
+  (reference: fused_qkv.py:596-662);
+* ``flash_prologue::fused_qkv_epilogue(x, weight, rmsnorm_weight, scales, sin, cos)
+  -> (q, k, v, q_proj, k_proj)``: the same projection with RMSNorm + RoPE + Q
+  scale applied to Q and K inside the GEMM epilogue, plus the pre-prologue
+  BF16 projections the backward uses (reference: fused_qkv.py:698-878, which
+  runs a GEMM, two copies and a separate prologue launch).
+
+``weight`` is the nn.Linear weight ``[3*H*D, hidden]`` with rows Q heads | K
+heads | V heads; D is taken from ``rmsnorm_weight`` (the reference hard-codes
+64, fused_qkv.py:606-607); H = weight.shape[0] // (3 * D). The projection is
+rounded to BF16 before the prologue, as a BF16 linear layer followed by the
+prologue would do. Backward: the prologue backward kernel on the saved
+projections, then dX = dP @ W and dW = dP^T @ X as plain library GEMMs.
+"""
+from typing import Tuple
+
+import torch
+
+from . import _lib
+from .fused_epilogue import _DeviceGuard, _ensure_4d, _table, qknorm_rope_scale_cute_backward_op
+
+BN_TILE = 256
+
+
+def _dims(x: torch.Tensor, weight: torch.Tensor, head_dim: int):
+    if x.ndim != 3 or weight.ndim != 2 or x.shape[2] != weight.shape[1]:
+        raise ValueError("x must be [B, N, hidden] and weight [3*H*D, hidden]")
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError("the fused QKV GEMM takes BF16 x and weight")
+    if head_dim not in (64, 128) or weight.shape[0] % (3 * head_dim):
+        raise ValueError("weight rows must be 3 * H * D with D in (64, 128)")
+    B, N, hidden = (int(s) for s in x.shape)
+    H = int(weight.shape[0]) // (3 * head_dim)
+    if (H * head_dim) % BN_TILE or hidden % 64:
+        raise ValueError("H * D must be a multiple of 256 and hidden a multiple of 64")
+    return B, N, hidden, H
+
+
+def _launch(x, weight, head_dim, outs, raws, rmsnorm_weight=None, scales=None, sin=None, cos=None,
+            eps=1e-5):
+    B, N, hidden, H = _dims(x, weight, head_dim)
+    if B * N == 0:
+        return
+    x2 = x.reshape(B * N, hidden)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    w2 = weight if weight.is_contiguous() else weight.contiguous()
+    lib = _lib.load()
+    apply = rmsnorm_weight is not None
+    if apply:
+        sin4, sin_str = _table(sin, B, N, head_dim // 2)
+        cos4, cos_str = _table(cos, B, N, head_dim // 2)
+        if sin_str[2] != 1 or sin4.data_ptr() % 16 or sin_str[1] % 4 or sin_str[0] % 4:
+            sin4 = sin4.contiguous()
+            sin_str = (sin4.stride(0) if sin4.shape[0] > 1 else 0,
+                       sin4.stride(2) if sin4.shape[2] > 1 else 0, 1)
+        if cos_str[2] != 1 or cos4.data_ptr() % 16 or cos_str[1] % 4 or cos_str[0] % 4:
+            cos4 = cos4.contiguous()
+            cos_str = (cos4.stride(0) if cos4.shape[0] > 1 else 0,
+                       cos4.stride(2) if cos4.shape[2] > 1 else 0, 1)
+        w = rmsnorm_weight.contiguous()
+        s = scales.contiguous()
+        tab = (_lib.ptr(w), _lib.ptr(s), _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4),
+               _lib.strides3(cos_str))
+    else:
+        null = _lib.ctypes.c_void_p(0)
+        tab = (null, null, null, None, null, None)
+    with _DeviceGuard(x.device):
+        status = lib.flash_prologue_qkv_gemm_fwd(
+            _lib.ptr(x2), _lib.ptr(w2), B * N, hidden, H, head_dim, N, *tab,
+            _lib.ptr(outs[0]), _lib.ptr(outs[1]), _lib.ptr(outs[2]),
+            _lib.ptr(raws[0]) if raws[0] is not None else None,
+            _lib.ptr(raws[1]) if raws[1] is not None else None,
+            float(eps), 1 if apply else 0, _lib.stream_of(x.device))
+    _lib.check(status, "flash_prologue_qkv_gemm_fwd")
+
+
+def _empty_bhnd(x, H, head_dim):
+    B, N = x.shape[0], x.shape[1]
+    return torch.empty((B, H, N, head_dim), dtype=torch.bfloat16, device=x.device)
+
+
+# The GEMM-only op has no rmsnorm_weight to read D from; like the reference
+# (fused_qkv.py:606-607) it splits the projection into heads of 64.
+GEMM_ONLY_HEAD_DIM = 64
+
+
+@torch.library.custom_op("flash_prologue::fused_qkv", mutates_args=())
+def fused_qkv_op(x: torch.Tensor, weight: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    head_dim = GEMM_ONLY_HEAD_DIM
+    _, _, _, H = _dims(x, weight, head_dim)
+    outs = [_empty_bhnd(x, H, head_dim) for _ in range(3)]
+    _launch(x, weight, head_dim, outs, (None, None))
+    return outs[0], outs[1], outs[2]
+
+
+@fused_qkv_op.register_fake
+def _fused_qkv_fake(x, weight):
+    head_dim = GEMM_ONLY_HEAD_DIM
+    H = weight.shape[0] // (3 * head_dim)
+    return tuple(torch.empty((x.shape[0], H, x.shape[1], head_dim), dtype=x.dtype, device=x.device)
+                 for _ in range(3))
+
+
+def _linear_backward(dq, dk, dv, weight, x):
+    """dX = dP W, dW = dP^T X for P = X W^T split into [B, H, N, D] heads."""
+    B, H, N, D = dq.shape
+    dp = torch.stack((dq, dk, dv), dim=0).permute(1, 3, 0, 2, 4).reshape(B * N, 3 * H * D)
+    x2 = x.reshape(B * N, -1)
+    grad_x = (dp @ weight).reshape(x.shape)
+    grad_w = dp.t() @ x2
+    return grad_x, grad_w
+
+
+def _fused_qkv_setup(ctx, inputs, output):
+    x, weight = inputs
+    ctx.save_for_backward(x, weight)
+
+
+def _fused_qkv_backward(ctx, gq, gk, gv):
+    x, weight = ctx.saved_tensors
+    return _linear_backward(gq, gk, gv, weight, x)
+
+
+torch.library.register_autograd("flash_prologue::fused_qkv", _fused_qkv_backward,
+                                setup_context=_fused_qkv_setup)
+
+
+@torch.library.custom_op("flash_prologue::fused_qkv_epilogue", mutates_args=())
+def fused_qkv_epilogue_op(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    rmsnorm_weight: torch.Tensor,
+    scales: torch.Tensor,
+    sin: torch.Tensor,
+    cos: torch.Tensor,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    head_dim = int(rmsnorm_weight.shape[-1])
+    _, _, _, H = _dims(x, weight, head_dim)
+    if tuple(rmsnorm_weight.shape) != (2, 1, head_dim) or scales.numel() != H:
+        raise ValueError("weight must be [2,1,D], log-scales must be [H,1,1]")
+    for t in (rmsnorm_weight, scales, sin, cos):
+        if t.dtype != torch.float32:
+            raise ValueError("weights, log-scales, and sin/cos must be FP32")
+    outs = [_empty_bhnd(x, H, head_dim) for _ in range(3)]
+    raws = [_empty_bhnd(x, H, head_dim) for _ in range(2)]
+    _launch(x, weight, head_dim, outs, raws, rmsnorm_weight, scales, sin, cos)
+    return outs[0], outs[1], outs[2], raws[0], raws[1]
+
+
+@fused_qkv_epilogue_op.register_fake
+def _fused_qkv_epilogue_fake(x, weight, rmsnorm_weight, scales, sin, cos):
+    head_dim = rmsnorm_weight.shape[-1]
+    H = weight.shape[0] // (3 * head_dim)
+    return tuple(torch.empty((x.shape[0], H, x.shape[1], head_dim), dtype=x.dtype, device=x.device)
+                 for _ in range(5))
+
+
+def _fused_qkv_epilogue_setup(ctx, inputs, output):
+    x, weight, rmsnorm_weight, scales, sin, cos = inputs
+    _, _, _, q_proj, k_proj = output
+    ctx.save_for_backward(x, weight, rmsnorm_weight, scales, sin, cos, q_proj, k_proj)
+
+
+def _fused_qkv_epilogue_backward(ctx, gq, gk, gv, g_qproj, g_kproj):
+    x, weight, rmsnorm_weight, scales, sin, cos, q_proj, k_proj = ctx.saved_tensors
+    B, H, N, D = q_proj.shape
+    sin4 = _ensure_4d(sin).expand(B, 1, N, D // 2)
+    cos4 = _ensure_4d(cos).expand(B, 1, N, D // 2)
+    dq, dk, dw, ds = qknorm_rope_scale_cute_backward_op(q_proj, k_proj, rmsnorm_weight, scales,
+                                                        sin4, cos4, gq, gk)
+    # The saved projections are outputs for the backward only; as in the
+    # reference (fused_qkv.py:847-867) gradients arriving on them are ignored.
+    grad_x, grad_w = _linear_backward(dq, dk, gv, weight, x)
+    return grad_x, grad_w, dw, ds, None, None
+
+
+torch.library.register_autograd("flash_prologue::fused_qkv_epilogue", _fused_qkv_epilogue_backward,
+                                setup_context=_fused_qkv_epilogue_setup)

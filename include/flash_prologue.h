@@ -128,6 +128,32 @@ FLASH_PROLOGUE_API int flash_prologue_bwd(const void* q, const int64_t q_strides
                        float eps, int dtype, void* stream);
 
 /*
+ * Fused QKV projection GEMM with the prologue in its epilogue (tcgen05 tensor
+ * cores, TMEM accumulators, TMA-fed). x: [M, K] BF16 row-major (M = B * S
+ * tokens); w: [3*H*D, K] BF16 row-major (nn.Linear layout, rows Q | K | V
+ * heads). Computes P = x * w^T, rounds P to BF16, and writes q_out, k_out,
+ * v_out as contiguous [B, H, S, D] BF16. With apply_prologue != 0, Q and K get
+ * RMSNorm (rmsnorm_weight [2,1,D]), split-half RoPE (sin/cos FP32 indexed
+ * [b, s, j] through sin_strides/cos_strides with j stride 1) and Q is
+ * multiplied by exp(scales[h]); q_proj/k_proj (optional, may be NULL) receive
+ * the BF16 projections before the prologue. With apply_prologue == 0 the
+ * prologue arguments may be NULL and Q/K are the plain projections.
+ * Requirements: D in {64, 128}; K % 64 == 0; (H*D) % 256 == 0; M % S == 0;
+ * x, w and outputs 16-byte aligned.
+ * Replaces flash_prologue::fused_qkv (flash_attn_prologue/fused_qkv.py:596-662)
+ * and flash_prologue::fused_qkv_epilogue (fused_qkv.py:698-878: GEMM launch,
+ * two copies and an in-place prologue launch), one kernel for both.
+ */
+FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(const void* x, const void* w,
+                       int64_t M, int64_t K, int64_t H, int64_t D, int64_t S,
+                       const float* rmsnorm_weight, const float* scales,
+                       const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3],
+                       void* q_out, void* k_out, void* v_out,
+                       void* q_proj, void* k_proj,
+                       float eps, int apply_prologue, void* stream);
+
+/*
  * Backward prologue that allocates nothing: the same computation and results
  * as flash_prologue_bwd, without the `workspace` arguments. For callers that
  * cannot allocate device memory per call (runtimes that plan all device memory
