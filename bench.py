@@ -140,7 +140,8 @@ def dist_setup(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     return world, rank, local
 
 
@@ -305,8 +306,109 @@ def run_ours(args, world, rank, local):
                                 "kind": "port",
                                 "sample": f"{args.cpu_tokens} tokens of C2 fwd+bwd, median of "
                                           f"{args.cpu_reps}, torch eager CPU port of native"}
+    if rank == 0 and world == 1 and not args.no_extras:
+        line["other_configs"] = run_extras(device)
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def _event_ms(fn, steps, warmup=3):
+    """Mean CUDA-event time of fn() on the current stream (inputs resident in HBM)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def run_extras(device, steps=20):
+    """The other benchmark configurations, timed on one GPU (reported beside the headline).
+
+    C1 packed fwd [4096, 4, 32] (launch-latency bound); C3 dense fwd
+    [8, 32, 8192, 128]; C4 packed bwd [262144, 8, 64]; C5 fused QKV GEMM +
+    prologue, X [65536, 2048] x W [6144, 2048] (H=16, D=128), beside the same
+    work as cuBLAS F.linear followed by this library's prologue kernel.
+    """
+    import flash_attn_prologue_b200 as fap
+    from flash_attn_prologue_b200 import qknorm_rope_scale
+    out = {}
+    g = torch.Generator(device=device).manual_seed(5)
+    peak, _ = measured_peak()
+    bf16_peak = _measured("bf16_tflops", 1590.0)
+
+    def hbm(name, nbytes, ms):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4),
+                     "pct_of_8tbs": round(100 * gbs / NOMINAL_HBM_GBS, 2), "algorithmic_bytes": nbytes}
+
+    # C1
+    T, H, D = 4096, 4, 32
+    q, k = (torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16) for _ in range(2))
+    sin, cos = rope_tables(torch.arange(T, device=device), D, 10000.0)
+    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
+    s = torch.zeros(H, 1, 1, device=device)
+    hbm("c1_fwd", T * (H * D * 2 * 4 + D * 4),
+        _event_ms(lambda: qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute"), steps))
+    # C3
+    B, H, S, D = 8, 32, 8192, 128
+    q, k = (torch.randn(B, H, S, D, generator=g, device=device).to(torch.bfloat16) for _ in range(2))
+    sin, cos = rope_tables(torch.arange(S, device=device), D, 500000.0)
+    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
+    s = torch.full((H, 1, 1), math.log(1 / math.sqrt(D)), device=device)
+    hbm("c3_fwd", B * H * S * D * 2 * 4 + S * D * 4,
+        _event_ms(lambda: qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute"), steps))
+    del q, k
+    # C4 (one rank's backward; the NCCL reduction is part of the multi-GPU step)
+    T, H, D = 262144, 8, 64
+    q, k, gq, gk = (torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16)
+                    for _ in range(4))
+    sin, cos = rope_tables(torch.arange(T, device=device), D, 10000.0)
+    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
+    s = 0.1 * torch.randn(H, 1, 1, generator=g, device=device)
+    bwd = torch.ops.flash_prologue.qknorm_rope_scale_cute_backward
+    q4, k4 = q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None]
+    g4q, g4k = gq.permute(1, 0, 2)[None], gk.permute(1, 0, 2)[None]
+    s4 = sin[None, None].expand(1, 1, T, D // 2)
+    c4 = cos[None, None].expand(1, 1, T, D // 2)
+    hbm("c4_bwd", T * (H * D * 2 * 6 + D * 4),
+        _event_ms(lambda: bwd(q4, k4, w, s, s4, c4, g4q, g4k, 1e-5), steps))
+    del q, k, gq, gk
+    # C5
+    T, hidden, H, D = 65536, 2048, 16, 128
+    x = torch.randn(1, T, hidden, generator=g, device=device).to(torch.bfloat16)
+    wq = (0.02 * torch.randn(3 * H * D, hidden, generator=g, device=device)).to(torch.bfloat16)
+    sin, cos = rope_tables(torch.arange(T, device=device), D, 10000.0)
+    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
+    s = 0.1 * torch.randn(H, 1, 1, generator=g, device=device)
+    flop = 2 * T * 3 * H * D * hidden
+    fused_ms = _event_ms(lambda: fap.fused_qkv_epilogue(x, wq, w, s, sin, cos), steps)
+
+    def unfused():
+        p = torch.nn.functional.linear(x[0], wq).view(T, 3, H, D)
+        return qknorm_rope_scale(p[:, 0], p[:, 1], w, s, sin, cos, backend="cute")
+    unfused_ms = _event_ms(unfused, steps)
+    linear_ms = _event_ms(lambda: torch.nn.functional.linear(x[0], wq), steps)
+    tf = flop / (fused_ms * 1e-3) / 1e12
+    out["c5_fused_qkv_gemm"] = {
+        "ms": round(fused_ms, 4), "tflops": round(tf, 1), "frac_of_measured_bf16": round(tf / bf16_peak, 4),
+        "bf16_peak_tflops": bf16_peak, "flop": flop,
+        "cublas_linear_then_prologue_kernel_ms": round(unfused_ms, 4),
+        "cublas_linear_alone_ms": round(linear_ms, 4),
+        "note": "fused = one tcgen05 kernel writing Q,K (prologue applied), V and the BF16 Q/K projections"}
+    return out
+
+
+def _measured(key, fallback):
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())[key])
+    except Exception:
+        return fallback
 
 
 def run_e2e(args, T, device, w, s, world):
@@ -371,6 +473,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=32768)
     ap.add_argument("--cpu-reps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the C1/C3/C4/C5 timings reported beside the headline")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

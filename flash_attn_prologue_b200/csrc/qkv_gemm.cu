@@ -188,24 +188,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------ epilogue ----------------------------------
     const int row = warp * 32 + lane;  // TMEM lane == tile row
+    // The token's sin/cos row (D/2 + D/2 floats), fetched for every Q/K tile
+    // before waiting for its accumulator so that the loads overlap the MMAs;
+    // both heads of the tile share it.
+    float sn[HALF], cs[HALF];
     uint32_t tcount = 0;
     for (int64_t tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++tcount) {
       const uint32_t abuf = tcount & 1;
-      if (!mbar_wait(&acc_full[abuf], (tcount >> 1) & 1)) break;
-      tc_fence_after();
       const int64_t m = (tile / a.n_tiles_n) * BM + row;
       const bool valid = m < a.M;
       const int64_t b = m / a.S, sp = m % a.S;
       const int64_t n0 = (tile % a.n_tiles_n) * BN;
+      const int seg = (int)(n0 / (a.H * D));  // the whole tile is Q (0), K (1) or V (2)
+      const bool prologue = a.apply_prologue && seg < 2;
+      if (prologue) {
+        if (valid) {
+          const float* srow = a.sin + b * a.sin_b + sp * a.sin_n;
+          const float* crow = a.cos + b * a.cos_b + sp * a.cos_n;
+#pragma unroll
+          for (int j = 0; j < HALF; j += 4) {
+            const float4 s4 = ldg4(srow + j), c4 = ldg4(crow + j);
+            sn[j] = s4.x; sn[j + 1] = s4.y; sn[j + 2] = s4.z; sn[j + 3] = s4.w;
+            cs[j] = c4.x; cs[j + 1] = c4.y; cs[j + 2] = c4.z; cs[j + 3] = c4.w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < HALF; ++j) { sn[j] = 0.f; cs[j] = 0.f; }
+        }
+      }
+      if (!mbar_wait(&acc_full[abuf], (tcount >> 1) & 1)) break;
+      tc_fence_after();
       const uint32_t tbase = tmem_base + abuf * kAccCols + ((uint32_t)(warp * 32) << 16);
       for (int hh = 0; hh < HEADS_PER_TILE; ++hh) {
-        const int64_t col = n0 + hh * D;
-        const int seg = (int)(col / (a.H * D));          // 0 Q, 1 K, 2 V
-        const int h = (int)((col % (a.H * D)) / D);
+        const int h = (int)(((n0 + hh * D) % (a.H * D)) / D);
         const uint32_t tcol = tbase + hh * D;
         const int64_t out_off = ((b * a.H + h) * a.S + sp) * D;
         __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out[seg]) + out_off;
-        if (seg == 2 || !a.apply_prologue) {
+        if (!prologue) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t v[32];
@@ -236,54 +255,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float2 r2 = splat2(r);
         const float2 e2 = splat2(seg == 0 ? e_s[h] : 1.f);
         const float* wrow = w_s + seg * D;
-        const float* srow = a.sin + b * a.sin_b + sp * a.sin_n;
-        const float* crow = a.cos + b * a.cos_b + sp * a.cos_n;
-        // Pass 2: columns j and j + D/2 of the head are in this thread.
-#pragma unroll 1
-        for (int c = 0; c < HALF / 32; ++c) {
-          uint32_t va[32], vb[32];
-          tmem_ld32(tcol + 32 * c, va);
-          tmem_ld32(tcol + HALF + 32 * c, vb);
+        // Pass 2, 16 columns at a time: columns j and j + D/2 of the head are
+        // in this thread; each product and sum rounds like the eager formulation.
+#pragma unroll
+        for (int g = 0; g < HALF / 16; ++g) {
+          uint32_t va[16], vb[16];
+          tmem_ld16(tcol + 16 * g, va);
+          tmem_ld16(tcol + HALF + 16 * g, vb);
           tmem_wait_ld();
-          uint32_t p1[16], p2[16];
+          uint32_t p1[8], p2[8];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {  // 8 columns at a time
-            float sn[8], cs[8];
-            if (valid) {
-              const float4 s0 = ldg4(srow + 32 * c + 8 * q), s1 = ldg4(srow + 32 * c + 8 * q + 4);
-              const float4 c0 = ldg4(crow + 32 * c + 8 * q), c1 = ldg4(crow + 32 * c + 8 * q + 4);
-              sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
-              sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-              cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
-              cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) { sn[j] = 0.f; cs[j] = 0.f; }
+          for (int i = 0; i < 8; ++i) {
+            const int j = 16 * g + 2 * i;  // column pair within the first half
+            const float2 x1 = round_bf16_pair(va[2 * i], va[2 * i + 1]);
+            const float2 x2 = round_bf16_pair(vb[2 * i], vb[2 * i + 1]);
+            const float2 wa = ld_pair(wrow, j / 2);
+            const float2 wb = ld_pair(wrow + HALF, j / 2);
+            const float2 c2 = make_float2(cs[j], cs[j + 1]);
+            const float2 s2 = make_float2(sn[j], sn[j + 1]);
+            const float2 y1 = __fmul2_rn(__fmul2_rn(x1, r2), wa);
+            const float2 y2 = __fmul2_rn(__fmul2_rn(x2, r2), wb);
+            float2 o1 = __fadd2_rn(__fmul2_rn(y1, c2), neg2(__fmul2_rn(y2, s2)));
+            float2 o2 = __fadd2_rn(__fmul2_rn(y2, c2), __fmul2_rn(y1, s2));
+            if (seg == 0) {
+              o1 = __fmul2_rn(o1, e2);
+              o2 = __fmul2_rn(o2, e2);
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int j = 8 * q + 2 * i;  // column pair within the chunk
-              const float2 x1 = round_bf16_pair(va[j], va[j + 1]);
-              const float2 x2 = round_bf16_pair(vb[j], vb[j + 1]);
-              const float2 wa = ld_pair(wrow + 32 * c, j / 2);
-              const float2 wb = ld_pair(wrow + HALF + 32 * c, j / 2);
-              const float2 c2 = make_float2(cs[2 * i], cs[2 * i + 1]);
-              const float2 s2 = make_float2(sn[2 * i], sn[2 * i + 1]);
-              const float2 y1 = __fmul2_rn(__fmul2_rn(x1, r2), wa);
-              const float2 y2 = __fmul2_rn(__fmul2_rn(x2, r2), wb);
-              float2 o1 = __fadd2_rn(__fmul2_rn(y1, c2), neg2(__fmul2_rn(y2, s2)));
-              float2 o2 = __fadd2_rn(__fmul2_rn(y2, c2), __fmul2_rn(y1, s2));
-              if (seg == 0) {
-                o1 = __fmul2_rn(o1, e2);
-                o2 = __fmul2_rn(o2, e2);
-              }
-              p1[j / 2] = pack_bf16(o1);
-              p2[j / 2] = pack_bf16(o2);
-            }
+            p1[i] = pack_bf16(o1);
+            p2[i] = pack_bf16(o2);
           }
           if (valid) {
-            store32(out + 32 * c, p1);
-            store32(out + HALF + 32 * c, p2);
+            uint4* d1 = reinterpret_cast<uint4*>(out + 16 * g);
+            uint4* d2 = reinterpret_cast<uint4*>(out + HALF + 16 * g);
+            d1[0] = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+            d1[1] = make_uint4(p1[4], p1[5], p1[6], p1[7]);
+            d2[0] = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+            d2[1] = make_uint4(p2[4], p2[5], p2[6], p2[7]);
           }
         }
       }
