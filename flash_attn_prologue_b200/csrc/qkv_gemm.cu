@@ -44,6 +44,10 @@ constexpr int kEpiWarps = 4;
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kGemmThreads = (kEpiWarps + 2) * 32;
+// Output staging: per epilogue warp, its 32 rows of one head as [32][128 B]
+// halves (64 BF16 columns each), 128-byte swizzled, written out by TMA stores.
+constexpr int kStageHalfBytes = 32 * 128;
+constexpr int kStagingPerWarp = 2 * kStageHalfBytes;  // up to D = 128
 
 struct GemmArgs {
   int64_t M, K, H, D, S;          // S = tokens per batch (M = B * S)
@@ -57,6 +61,13 @@ struct GemmArgs {
   void* raw[2];                   // optional BF16 q, k projections [B, H, S, D]
   float eps;
   int apply_prologue;
+  int tma_store;                  // 1: outputs through per-warp staging + TMA stores (S % 32 == 0)
+};
+
+// Tensor maps of the five outputs as 2-D [B*H*S rows, D columns] BF16 tensors
+// with a (64 x 32) box and 128-byte swizzle: q, k, v, raw q, raw k.
+struct OutMaps {
+  CUtensorMap m[5];
 };
 
 __device__ __forceinline__ float2 round_bf16_pair(uint32_t a, uint32_t b) {
@@ -91,19 +102,20 @@ template <int D>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     qkv_gemm_prologue_kernel(const __grid_constant__ CUtensorMap tm_x,
                              const __grid_constant__ CUtensorMap tm_w,
+                             const __grid_constant__ OutMaps om,
                              const __grid_constant__ GemmArgs a) {
   constexpr int HALF = D / 2;
   constexpr int HEADS_PER_TILE = BN / D;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  unsigned char* staging = smem + kStages * kStageBytes;  // [kEpiWarps][kStagingPerWarp]
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * kStagingPerWarp);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   float* w_s = reinterpret_cast<float*>(tmem_slot + 4);  // [2 * D]
-  float* e_s = w_s + 2 * D;                              // [H]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -124,7 +136,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   if (a.apply_prologue) {
     for (int i = threadIdx.x; i < 2 * D; i += kGemmThreads) w_s[i] = a.w[i];
-    for (int i = threadIdx.x; i < a.H; i += kGemmThreads) e_s[i] = (float)exp((double)a.scales[i]);
   }
   tc_fence_before();
   __syncthreads();
@@ -188,9 +199,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------ epilogue ----------------------------------
     const int row = warp * 32 + lane;  // TMEM lane == tile row
+    unsigned char* stage_w = staging + warp * kStagingPerWarp;
+    const bool staged = a.tma_store != 0;
+    // 16 output bytes (8 BF16 at column `col` of the head) of this thread's row:
+    // into the warp's swizzled staging tile, or straight to global memory.
+    auto emit16 = [&](__nv_bfloat16* grow, bool valid, int col, uint4 v) {
+      if (staged) {
+        unsigned char* half = stage_w + (col >> 6) * kStageHalfBytes;
+        const int chunk = (col & 63) >> 3;
+        *reinterpret_cast<uint4*>(half + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = v;
+      } else if (valid) {
+        *reinterpret_cast<uint4*>(grow + col) = v;
+      }
+    };
+    // Staged path: write the warp's 32 rows of one head to `map` at row0 ...
+    auto flush = [&](const CUtensorMap* map, int64_t row0) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        for (int half = 0; half < D / 64; ++half)
+          tma_store_2d(map, half * 64, (int32_t)row0, stage_w + half * kStageHalfBytes);
+        bulk_commit_group();
+      }
+    };
+    // ... and before refilling the staging tile, wait until those stores have read it.
+    auto reclaim = [&]() {
+      if (lane == 0) bulk_wait_group_read0();
+      __syncwarp();
+    };
     // The token's sin/cos row (D/2 + D/2 floats), fetched for every Q/K tile
     // before waiting for its accumulator so that the loads overlap the MMAs;
-    // both heads of the tile share it.
+    // every head of the tile shares it.
     float sn[HALF], cs[HALF];
     uint32_t tcount = 0;
     for (int64_t tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++tcount) {
@@ -198,6 +237,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int64_t m = (tile / a.n_tiles_n) * BM + row;
       const bool valid = m < a.M;
       const int64_t b = m / a.S, sp = m % a.S;
+      // First token of this warp's 32 rows (S % 32 == 0 on the staged path,
+      // so all 32 share its batch index).
+      const int64_t mw = (tile / a.n_tiles_n) * BM + warp * 32;
+      const int64_t bw = mw / a.S, spw = mw % a.S;
       const int64_t n0 = (tile % a.n_tiles_n) * BN;
       const int seg = (int)(n0 / (a.H * D));  // the whole tile is Q (0), K (1) or V (2)
       const bool prologue = a.apply_prologue && seg < 2;
@@ -223,19 +266,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int h = (int)(((n0 + hh * D) % (a.H * D)) / D);
         const uint32_t tcol = tbase + hh * D;
         const int64_t out_off = ((b * a.H + h) * a.S + sp) * D;
+        const int64_t row0 = (bw * a.H + h) * a.S + spw;  // staged path: first output row
         __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out[seg]) + out_off;
+        if (staged) reclaim();
         if (!prologue) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t v[32];
             tmem_ld32(tcol + 32 * c, v);
             tmem_wait_ld();
-            if (valid) store_chunk_rounded(out + 32 * c, v);
+            uint32_t p[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) p[i] = pack_bf16(round_bf16_pair(v[2 * i], v[2 * i + 1]));
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              emit16(out, valid, 32 * c + 8 * q, make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]));
           }
+          if (staged) flush(&om.m[seg], row0);
           continue;
         }
         // Pass 1: BF16 projection, optional raw store, sum of squares.
-        __nv_bfloat16* raw = a.raw[seg] ? static_cast<__nv_bfloat16*>(a.raw[seg]) + out_off : nullptr;
+        const bool want_raw = a.raw[seg] != nullptr;
+        __nv_bfloat16* raw = want_raw ? static_cast<__nv_bfloat16*>(a.raw[seg]) + out_off : nullptr;
         float2 acc = make_float2(0.f, 0.f);
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
@@ -249,11 +301,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             acc = __ffma2_rn(x, x, acc);  // squares of BF16 values are exact in FP32
             p[i] = pack_bf16(x);
           }
-          if (valid && raw) store32(raw + 32 * c, p);
+          if (want_raw) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              emit16(raw, valid, 32 * c + 8 * q, make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]));
+          }
+        }
+        if (want_raw && staged) {
+          flush(&om.m[3 + seg], row0);
+          reclaim();
         }
         const float r = inv_rms<D>(__fadd_rn(acc.x, acc.y), a.eps);
         const float2 r2 = splat2(r);
-        const float2 e2 = splat2(seg == 0 ? e_s[h] : 1.f);
+        const float2 e2 = splat2(seg == 0 ? (float)exp((double)a.scales[h]) : 1.f);
         const float* wrow = w_s + seg * D;
         // Pass 2, 16 columns at a time: columns j and j + D/2 of the head are
         // in this thread; each product and sum rounds like the eager formulation.
@@ -284,20 +344,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             p1[i] = pack_bf16(o1);
             p2[i] = pack_bf16(o2);
           }
-          if (valid) {
-            uint4* d1 = reinterpret_cast<uint4*>(out + 16 * g);
-            uint4* d2 = reinterpret_cast<uint4*>(out + HALF + 16 * g);
-            d1[0] = make_uint4(p1[0], p1[1], p1[2], p1[3]);
-            d1[1] = make_uint4(p1[4], p1[5], p1[6], p1[7]);
-            d2[0] = make_uint4(p2[0], p2[1], p2[2], p2[3]);
-            d2[1] = make_uint4(p2[4], p2[5], p2[6], p2[7]);
-          }
+          emit16(out, valid, 16 * g, make_uint4(p1[0], p1[1], p1[2], p1[3]));
+          emit16(out, valid, 16 * g + 8, make_uint4(p1[4], p1[5], p1[6], p1[7]));
+          emit16(out, valid, HALF + 16 * g, make_uint4(p2[0], p2[1], p2[2], p2[3]));
+          emit16(out, valid, HALF + 16 * g + 8, make_uint4(p2[4], p2[5], p2[6], p2[7]));
         }
+        if (staged) flush(&om.m[seg], row0);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[abuf]);
     }
+    // Every staged store must have completed before the CTA ends.
+    if (staged && lane == 0) bulk_wait_group0();
   }
 
   // Teardown: every warp arrives here (also after a timed-out wait).
@@ -346,22 +405,23 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-size_t gemm_smem_bytes(int64_t H, int64_t D) {
-  return 1024 + (size_t)kStages * kStageBytes + 256 + (size_t)(2 * D + H) * 4;
+size_t gemm_smem_bytes(int64_t D) {
+  return 1024 + (size_t)kStages * kStageBytes + (size_t)kEpiWarps * kStagingPerWarp + 256 +
+         (size_t)(2 * D) * 4;
 }
 
 template <int D>
-cudaError_t launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const GemmArgs& args,
-                        cudaStream_t stream) {
+cudaError_t launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const OutMaps& om,
+                        const GemmArgs& args, cudaStream_t stream) {
   const void* fn = reinterpret_cast<const void*>(&qkv_gemm_prologue_kernel<D>);
-  const size_t smem = gemm_smem_bytes(args.H, D);
+  const size_t smem = gemm_smem_bytes(D);
   cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
   int dev = 0, sms = 0;
   if ((err = cudaGetDevice(&dev)) != cudaSuccess) return err;
   if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return err;
   const int64_t grid = args.n_tiles < sms ? args.n_tiles : sms;
-  qkv_gemm_prologue_kernel<D><<<(unsigned)grid, kGemmThreads, smem, stream>>>(mx, mw, args);
+  qkv_gemm_prologue_kernel<D><<<(unsigned)grid, kGemmThreads, smem, stream>>>(mx, mw, om, args);
   return cudaGetLastError();
 }
 
@@ -393,7 +453,7 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(
   if (M == 0) return FLASH_PROLOGUE_OK;
   if (D != 64 && D != 128) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
   if (K % BK != 0 || (H * D) % BN != 0 || M % S != 0) return FLASH_PROLOGUE_ERR_UNSUPPORTED;
-  if (H > 512 || M >= (int64_t(1) << 31) || 3 * H * D >= (int64_t(1) << 31))
+  if (H > 512 || M * H >= (int64_t(1) << 31) || 3 * H * D >= (int64_t(1) << 31))
     return FLASH_PROLOGUE_ERR_UNSUPPORTED;
   if (!x || !w || !q_out || !k_out || !v_out) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   if (!al16(x) || !al16(w) || !al16(q_out) || !al16(k_out) || !al16(v_out) ||
@@ -422,8 +482,19 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(
   g.raw[0] = q_proj; g.raw[1] = k_proj;
   g.eps = eps;
   g.apply_prologue = apply_prologue ? 1 : 0;
+  // Outputs go through per-warp staging and TMA stores when every warp's 32
+  // token rows are contiguous in [B, H, S, D] (S a multiple of 32).
+  OutMaps om;
+  g.tma_store = (S % 32 == 0) ? 1 : 0;
+  if (g.tma_store) {
+    void* outs[5] = {q_out, k_out, v_out, q_proj ? q_proj : q_out, k_proj ? k_proj : k_out};
+    for (int i = 0; i < 5; ++i)
+      if (!make_map(&om.m[i], outs[i], M * H, D, 32)) return FLASH_PROLOGUE_ERR_CUDA;
+  } else {
+    for (int i = 0; i < 5; ++i) om.m[i] = mx;  // unused
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t err = (D == 64) ? launch_gemm<64>(mx, mw, g, s) : launch_gemm<128>(mx, mw, g, s);
+  cudaError_t err = (D == 64) ? launch_gemm<64>(mx, mw, om, g, s) : launch_gemm<128>(mx, mw, om, g, s);
   return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
 }
 
