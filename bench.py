@@ -379,6 +379,25 @@ def run_extras(device, steps=20):
     hbm("c4_bwd", T * (H * D * 2 * 6 + D * 4),
         _event_ms(lambda: bwd(q4, k4, w, s, s4, c4, g4q, g4k, 1e-5), steps))
     del q, k, gq, gk
+    # C2 through the inverse formulation (forward also stores r per row; the
+    # backward rebuilds rows from the outputs and r): strided views of the
+    # [T, 3, H, D] buffer, algorithmic bytes + 4 B per row of r.
+    T, H, D = T_TOKENS, HEADS, HEAD_DIM
+    buf = torch.randn(T, 3, H, D, generator=g, device=device).to(torch.bfloat16)
+    q4, k4 = (buf[:, i].permute(1, 0, 2)[None] for i in (0, 1))
+    g4q, g4k = (torch.randn(1, H, T, D, generator=g, device=device).to(torch.bfloat16) for _ in range(2))
+    sin, cos = rope_tables(torch.arange(T, device=device) % 4096, D, 10000.0)
+    s4, c4 = sin[None, None], cos[None, None]
+    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
+    s = 0.1 * torch.randn(H, 1, 1, generator=g, device=device)
+    inv_fwd = torch.ops.flash_prologue.qknorm_rope_scale_cute_inverse
+    inv_bwd = torch.ops.flash_prologue.qknorm_rope_scale_cute_inverse_backward
+    qo, ko, rq, rk = inv_fwd(q4, k4, w, s, s4, c4, 1e-5)
+    hbm("c2_inverse_fwd", T * (H * D * 2 * 4 + D * 4 + 2 * H * 4),
+        _event_ms(lambda: inv_fwd(q4, k4, w, s, s4, c4, 1e-5), steps))
+    hbm("c2_inverse_bwd", T * (H * D * 2 * 6 + D * 4 + 2 * H * 4),
+        _event_ms(lambda: inv_bwd(qo, ko, w, s, s4, c4, g4q, g4k, rq, rk, 1e-5), steps))
+    del buf, q4, k4, g4q, g4k, qo, ko, rq, rk
     # C5
     T, hidden, H, D = 65536, 2048, 16, 128
     x = torch.randn(1, T, hidden, generator=g, device=device).to(torch.bfloat16)

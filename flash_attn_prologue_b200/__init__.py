@@ -16,6 +16,9 @@ __version__ = "0.2.0"
 _LAZY = {
     "qknorm_rope_scale_cute_op": ("fused_epilogue", "qknorm_rope_scale_cute_op"),
     "qknorm_rope_scale_cute_backward_op": ("fused_epilogue", "qknorm_rope_scale_cute_backward_op"),
+    "qknorm_rope_scale_cute_inverse_op": ("fused_epilogue", "qknorm_rope_scale_cute_inverse_op"),
+    "qknorm_rope_scale_cute_inverse_backward_op": ("fused_epilogue",
+                                                   "qknorm_rope_scale_cute_inverse_backward_op"),
     "fused_qkv": ("fused_qkv", "fused_qkv_op"),
     "fused_qkv_epilogue": ("fused_qkv", "fused_qkv_epilogue_op"),
 }

@@ -37,6 +37,13 @@ SIGNATURES = {
     "flash_prologue_fwd": ([_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
                             _vp, _i64p, _vp, _i64p, _i64, _i64, _i64, _i64,
                             ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
+    "flash_prologue_inverse_fwd": ([_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
+                                    _vp, _vp, _vp, _i64p, _vp, _i64p, _i64, _i64, _i64, _i64,
+                                    ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
+    "flash_prologue_inverse_bwd": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _vp, _vp, _i64p,
+                                    _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p,
+                                    _vp, _vp, _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64,
+                                    ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
     "flash_prologue_bwd_workspace_size": ([_i64, _i64, _i64, _i64, ctypes.c_int,
                                            ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "flash_prologue_bwd_noalloc": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,

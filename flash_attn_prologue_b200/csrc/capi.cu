@@ -260,16 +260,25 @@ const char* flash_prologue_status_string(int status) {
 
 int flash_prologue_version(void) { return 100; }
 
-int flash_prologue_fwd(const void* q, const int64_t q_strides[4], const void* k,
-                       const int64_t k_strides[4], void* q_out, const int64_t q_out_strides[4],
-                       void* k_out, const int64_t k_out_strides[4], const float* rmsnorm_weight,
-                       const float* scales, const float* sin, const int64_t sin_strides[3],
-                       const float* cos, const int64_t cos_strides[3], int64_t B, int64_t H,
-                       int64_t N, int64_t D, float eps, int dtype, void* stream) {
+}  // extern "C"
+
+namespace {
+
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+// Forward; rms_q / rms_k (both null, or both FP32 [B, H, N]) receive r per row.
+int fwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+             void* q_out, const int64_t q_out_strides[4], void* k_out,
+             const int64_t k_out_strides[4], float* rms_q, float* rms_k,
+             const float* rmsnorm_weight, const float* scales, const float* sin,
+             const int64_t sin_strides[3], const float* cos, const int64_t cos_strides[3],
+             int64_t B, int64_t H, int64_t N, int64_t D, float eps, int dtype, void* stream) {
   int st = common_checks(q, q_strides, k, k_strides, rmsnorm_weight, scales, sin, sin_strides, cos,
                          cos_strides, B, H, N, D, eps, dtype);
   if (st != FLASH_PROLOGUE_OK || B * H * N == 0) return st;
   if (!q_out || !k_out || !q_out_strides || !k_out_strides) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  if ((rms_q == nullptr) != (rms_k == nullptr)) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  if ((rms_q && !aligned4(rms_q)) || (rms_k && !aligned4(rms_k))) return FLASH_PROLOGUE_ERR_ALIGNMENT;
   st = check_view(q_out_strides, B, H, N);
   if (st == FLASH_PROLOGUE_OK) st = check_view(k_out_strides, B, H, N);
   if (st != FLASH_PROLOGUE_OK) return st;
@@ -289,6 +298,7 @@ int flash_prologue_fwd(const void* q, const int64_t q_strides[4], const void* k,
       t.so[0] = rows(q_out_strides); t.so[1] = rows(k_out_strides);
       t.w = rmsnorm_weight; t.scales = scales; t.sin = sin; t.cos = cos;
       t.sin_b = sin_strides[0]; t.cos_b = cos_strides[0];
+      t.rms[0] = rms_q; t.rms[1] = rms_k;
       t.B = B; t.N = N; t.H = (int)H; t.eps = eps;
       t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kFwdStages);
       cudaError_t err = launch_fwd_tma(t, dtype, (int)D, s);
@@ -301,17 +311,47 @@ int flash_prologue_fwd(const void* q, const int64_t q_strides[4], const void* k,
   a.sy[0] = rows(q_out_strides); a.sy[1] = rows(k_out_strides);
   a.w = rmsnorm_weight; a.scales = scales; a.sin = sin; a.cos = cos;
   a.ssin = table(sin_strides); a.scos = table(cos_strides);
+  a.rms[0] = rms_q; a.rms[1] = rms_k;
   a.B = B; a.N = N; a.H = (int)H; a.eps = eps;
   a.g = plan_geometry(B, H, N, (int)D, heads_inner);
   cudaError_t err = launch_fwd(a, dtype, (int)D, vec, s);
   return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
 }
 
-static int bwd_plan(int64_t B, int64_t H, int64_t N, int64_t D, int dtype, bool vec,
-                    bool heads_inner, Geometry* g, int64_t* grid) {
+int bwd_plan(int64_t B, int64_t H, int64_t N, int64_t D, int dtype, bool vec, bool heads_inner,
+             bool inv, Geometry* g, int64_t* grid) {
   *g = plan_geometry(B, H, N, (int)D, heads_inner);
-  *grid = bwd_grid(*g, (int)H, (int)D, dtype, vec);
+  *grid = bwd_grid(*g, (int)H, (int)D, dtype, vec, inv);
   return *grid > 0 ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+int flash_prologue_fwd(const void* q, const int64_t q_strides[4], const void* k,
+                       const int64_t k_strides[4], void* q_out, const int64_t q_out_strides[4],
+                       void* k_out, const int64_t k_out_strides[4], const float* rmsnorm_weight,
+                       const float* scales, const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3], int64_t B, int64_t H,
+                       int64_t N, int64_t D, float eps, int dtype, void* stream) {
+  return fwd_impl(q, q_strides, k, k_strides, q_out, q_out_strides, k_out, k_out_strides, nullptr,
+                  nullptr, rmsnorm_weight, scales, sin, sin_strides, cos, cos_strides, B, H, N, D,
+                  eps, dtype, stream);
+}
+
+int flash_prologue_inverse_fwd(const void* q, const int64_t q_strides[4], const void* k,
+                               const int64_t k_strides[4], void* q_out,
+                               const int64_t q_out_strides[4], void* k_out,
+                               const int64_t k_out_strides[4], float* rms_q, float* rms_k,
+                               const float* rmsnorm_weight, const float* scales, const float* sin,
+                               const int64_t sin_strides[3], const float* cos,
+                               const int64_t cos_strides[3], int64_t B, int64_t H, int64_t N,
+                               int64_t D, float eps, int dtype, void* stream) {
+  if (B * H * N > 0 && (!rms_q || !rms_k)) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  return fwd_impl(q, q_strides, k, k_strides, q_out, q_out_strides, k_out, k_out_strides, rms_q,
+                  rms_k, rmsnorm_weight, scales, sin, sin_strides, cos, cos_strides, B, H, N, D,
+                  eps, dtype, stream);
 }
 
 int flash_prologue_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D, int dtype,
@@ -324,33 +364,42 @@ int flash_prologue_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D
   if (B * H * N == 0) return FLASH_PROLOGUE_OK;
   // The grid (and so the workspace) is the largest of the layouts and vector
   // widths the call may pick, so one size serves every stride pattern.
+  // The inverse backward's kernels are included, so the same size serves
+  // flash_prologue_inverse_bwd.
   int64_t worst = 0;
-  for (int hi = 0; hi < 2; ++hi) {
-    for (int v = 0; v < 2; ++v) {
-      Geometry g;
-      int64_t grid;
-      int st = bwd_plan(B, H, N, D, dtype, v != 0, hi != 0, &g, &grid);
-      if (st != FLASH_PROLOGUE_OK) return st;
-      if (grid > worst) worst = grid;
+  for (int inv = 0; inv < 2; ++inv) {
+    for (int hi = 0; hi < 2; ++hi) {
+      for (int v = 0; v < 2; ++v) {
+        Geometry g;
+        int64_t grid;
+        int st = bwd_plan(B, H, N, D, dtype, v != 0, hi != 0, inv != 0, &g, &grid);
+        if (st != FLASH_PROLOGUE_OK) return st;
+        if (grid > worst) worst = grid;
+      }
+      const int64_t tgrid = tma_grid(true, plan_tma(B, H, N, D, dtype, hi != 0, kBwdStages),
+                                     (int)H, (int)D, dtype, inv != 0);
+      if (tgrid <= 0) return FLASH_PROLOGUE_ERR_CUDA;
+      if (tgrid > worst) worst = tgrid;
     }
-    const int64_t tgrid = tma_grid(true, plan_tma(B, H, N, D, dtype, hi != 0, kBwdStages), (int)H,
-                                   (int)D, dtype);
-    if (tgrid <= 0) return FLASH_PROLOGUE_ERR_CUDA;
-    if (tgrid > worst) worst = tgrid;
   }
   *bytes = (size_t)worst * (size_t)(2 * D + H) * sizeof(float);
   return FLASH_PROLOGUE_OK;
 }
 
-int flash_prologue_bwd(const void* q, const int64_t q_strides[4], const void* k,
-                       const int64_t k_strides[4], const float* rmsnorm_weight,
-                       const float* scales, const float* sin, const int64_t sin_strides[3],
-                       const float* cos, const int64_t cos_strides[3], const void* grad_q_out,
-                       const int64_t gq_strides[4], const void* grad_k_out,
-                       const int64_t gk_strides[4], void* grad_q, const int64_t dq_strides[4],
-                       void* grad_k, const int64_t dk_strides[4], float* grad_rmsnorm_weight,
-                       float* grad_scales, void* workspace, size_t workspace_bytes, int64_t B,
-                       int64_t H, int64_t N, int64_t D, float eps, int dtype, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Backward. With inv, q / k are the forward outputs and rms_q / rms_k their saved r.
+int bwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+             const float* rms_q, const float* rms_k, bool inv, const float* rmsnorm_weight,
+             const float* scales, const float* sin, const int64_t sin_strides[3], const float* cos,
+             const int64_t cos_strides[3], const void* grad_q_out, const int64_t gq_strides[4],
+             const void* grad_k_out, const int64_t gk_strides[4], void* grad_q,
+             const int64_t dq_strides[4], void* grad_k, const int64_t dk_strides[4],
+             float* grad_rmsnorm_weight, float* grad_scales, void* workspace,
+             size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D, float eps,
+             int dtype, void* stream) {
   int st = common_checks(q, q_strides, k, k_strides, rmsnorm_weight, scales, sin, sin_strides, cos,
                          cos_strides, B, H, N, D, eps, dtype);
   if (st != FLASH_PROLOGUE_OK) return st;
@@ -366,6 +415,10 @@ int flash_prologue_bwd(const void* q, const int64_t q_strides[4], const void* k,
   if (!grad_q_out || !grad_k_out || !grad_q || !grad_k || !gq_strides || !gk_strides ||
       !dq_strides || !dk_strides)
     return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  if (inv) {
+    if (!rms_q || !rms_k) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+    if (!aligned4(rms_q) || !aligned4(rms_k)) return FLASH_PROLOGUE_ERR_ALIGNMENT;
+  }
   // Upstream gradients are only read, so broadcast (stride-0) views such as the
   // gradient of a sum() are read in place; their d stride must still be 1.
   if (gq_strides[3] != 1 || gk_strides[3] != 1) return FLASH_PROLOGUE_ERR_CHANNEL_STRIDE;
@@ -387,7 +440,7 @@ int flash_prologue_bwd(const void* q, const int64_t q_strides[4], const void* k,
         tma_tensor_ok(grad_k_out, gk_strides, D, es, heads_inner, &t.in[3]) &&
         tma_table_ok(sin, sin_strides, N, D) && tma_table_ok(cos, cos_strides, N, D)) {
       t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kBwdStages);
-      const int64_t tgrid = tma_grid(true, t.p, (int)H, (int)D, dtype);
+      const int64_t tgrid = tma_grid(true, t.p, (int)H, (int)D, dtype, inv);
       if (tgrid <= 0) return FLASH_PROLOGUE_ERR_CUDA;
       const size_t tneed = (size_t)tgrid * (size_t)(2 * D + H) * sizeof(float);
       if (!workspace || workspace_bytes < tneed || !aligned16(workspace))
@@ -397,14 +450,15 @@ int flash_prologue_bwd(const void* q, const int64_t q_strides[4], const void* k,
       t.w = rmsnorm_weight; t.scales = scales; t.sin = sin; t.cos = cos;
       t.sin_b = sin_strides[0]; t.cos_b = cos_strides[0];
       t.partials = static_cast<float*>(workspace);
+      t.rms[0] = rms_q; t.rms[1] = rms_k;
       t.B = B; t.N = N; t.H = (int)H; t.eps = eps;
-      cudaError_t err = launch_bwd_tma(t, grad_rmsnorm_weight, grad_scales, dtype, (int)D, s);
+      cudaError_t err = launch_bwd_tma(t, grad_rmsnorm_weight, grad_scales, dtype, (int)D, inv, s);
       return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
     }
   }
   Geometry g;
   int64_t grid;
-  st = bwd_plan(B, H, N, D, dtype, vec, heads_inner, &g, &grid);
+  st = bwd_plan(B, H, N, D, dtype, vec, heads_inner, inv, &g, &grid);
   if (st != FLASH_PROLOGUE_OK) return st;
   const size_t need = (size_t)grid * (size_t)(2 * D + H) * sizeof(float);
   if (!workspace || workspace_bytes < need || !aligned16(workspace)) return FLASH_PROLOGUE_ERR_WORKSPACE;
@@ -418,10 +472,49 @@ int flash_prologue_bwd(const void* q, const int64_t q_strides[4], const void* k,
   a.w = rmsnorm_weight; a.scales = scales; a.sin = sin; a.cos = cos;
   a.ssin = table(sin_strides); a.scos = table(cos_strides);
   a.partials = static_cast<float*>(workspace);
+  a.rms[0] = rms_q; a.rms[1] = rms_k;
   a.B = B; a.N = N; a.H = (int)H; a.eps = eps;
   a.g = g;
-  cudaError_t err = launch_bwd(a, grad_rmsnorm_weight, grad_scales, dtype, (int)D, vec, s);
+  cudaError_t err = launch_bwd(a, grad_rmsnorm_weight, grad_scales, dtype, (int)D, vec, inv, s);
   return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+int flash_prologue_bwd(const void* q, const int64_t q_strides[4], const void* k,
+                       const int64_t k_strides[4], const float* rmsnorm_weight,
+                       const float* scales, const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3], const void* grad_q_out,
+                       const int64_t gq_strides[4], const void* grad_k_out,
+                       const int64_t gk_strides[4], void* grad_q, const int64_t dq_strides[4],
+                       void* grad_k, const int64_t dk_strides[4], float* grad_rmsnorm_weight,
+                       float* grad_scales, void* workspace, size_t workspace_bytes, int64_t B,
+                       int64_t H, int64_t N, int64_t D, float eps, int dtype, void* stream) {
+  return bwd_impl(q, q_strides, k, k_strides, nullptr, nullptr, false, rmsnorm_weight, scales, sin,
+                  sin_strides, cos, cos_strides, grad_q_out, gq_strides, grad_k_out, gk_strides,
+                  grad_q, dq_strides, grad_k, dk_strides, grad_rmsnorm_weight, grad_scales,
+                  workspace, workspace_bytes, B, H, N, D, eps, dtype, stream);
+}
+
+int flash_prologue_inverse_bwd(const void* q_out, const int64_t q_out_strides[4],
+                               const void* k_out, const int64_t k_out_strides[4],
+                               const float* rms_q, const float* rms_k,
+                               const float* rmsnorm_weight, const float* scales, const float* sin,
+                               const int64_t sin_strides[3], const float* cos,
+                               const int64_t cos_strides[3], const void* grad_q_out,
+                               const int64_t gq_strides[4], const void* grad_k_out,
+                               const int64_t gk_strides[4], void* grad_q,
+                               const int64_t dq_strides[4], void* grad_k,
+                               const int64_t dk_strides[4], float* grad_rmsnorm_weight,
+                               float* grad_scales, void* workspace, size_t workspace_bytes,
+                               int64_t B, int64_t H, int64_t N, int64_t D, float eps, int dtype,
+                               void* stream) {
+  return bwd_impl(q_out, q_out_strides, k_out, k_out_strides, rms_q, rms_k, true, rmsnorm_weight,
+                  scales, sin, sin_strides, cos, cos_strides, grad_q_out, gq_strides, grad_k_out,
+                  gk_strides, grad_q, dq_strides, grad_k, dk_strides, grad_rmsnorm_weight,
+                  grad_scales, workspace, workspace_bytes, B, H, N, D, eps, dtype, stream);
 }
 
 }  // extern "C"

@@ -17,11 +17,15 @@
 // register/shared partials that are combined in a fixed order into one
 // [2*D + H] partial per CTA, and a second kernel sums the CTA partials in CTA
 // order. The result is bit-identical on every run with the same grid.
+//
+// INV = true is the inverse backward (fused_epilogue.py:2200-2300): x[] hold the
+// forward outputs and rms[] the saved r of every row; the normalised row n is
+// rebuilt from them (inv_lane_normed) instead of being recomputed from q and k.
 #include "prologue_host.h"
 
 namespace flash_prologue {
 
-template <typename T, int D, bool VEC>
+template <typename T, int D, bool VEC, bool INV>
 __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a) {
   constexpr int L = D / 16;
   constexpr int HALF = D / 2;
@@ -31,9 +35,15 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
   float* e_s = w_s + 2 * D;                // [H]
   float* ds_s = e_s + a.H;                 // [kWarps][H]
   float* dw_s = ds_s + kWarps * a.H;       // [kWarps][D]
+  float* iw_s = dw_s + kWarps * D;         // INV: [2 * D] 1 / w
+  float* ie_s = iw_s + 2 * D;              // INV: [H] 1 / exp(scales)
   for (int i = threadIdx.x; i < 2 * D; i += kThreads) w_s[i] = a.w[i];
   for (int i = threadIdx.x; i < a.H; i += kThreads) e_s[i] = (float)exp((double)a.scales[i]);
   for (int i = threadIdx.x; i < kWarps * a.H; i += kThreads) ds_s[i] = 0.f;
+  if constexpr (INV) {
+    for (int i = threadIdx.x; i < 2 * D; i += kThreads) iw_s[i] = __frcp_rn(a.w[i]);
+    for (int i = threadIdx.x; i < a.H; i += kThreads) ie_s[i] = (float)(1.0 / exp((double)a.scales[i]));
+  }
   __syncthreads();
 
   // The host makes the grid even (or equal to the even item count), so every
@@ -44,6 +54,8 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
   T* db = static_cast<T*>(a.dx[t]);
   const RowStrides sx = a.sx[t], sg = a.sgy[t], sd = a.sdx[t];
   const float* w = w_s + t * D;
+  const float* iw = iw_s + t * D;
+  const float* rms = INV ? a.rms[t] : nullptr;
 
   int c, hs, ps;
   thread_slots(a.g, threadIdx.x, c, hs, ps);
@@ -102,10 +114,24 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
         for (int k = 0; k < Chunk<T>::kWords; ++k) { x1.w[k] = 0; x2.w[k] = 0; g1.w[k] = 0; g2.w[k] = 0; }
       }
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
-      const float r = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
       float2 dnw1[kPairs], dnw2[kPairs];
-      const float dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, r, e, t == 0, w + j0,
-                                                    w + HALF + j0, sn, cs, acc1p, acc2p, dnw1, dnw2));
+      float2 n1[kPairs], n2[kPairs];  // INV: the rebuilt normalised row
+      float r, dsum;
+      if constexpr (INV) {
+        r = ok ? __ldg(rms + (b * a.H + h) * a.N + n) : 0.f;
+        if (ok) {
+          inv_lane_normed(x1, x2, t == 0, ie_s[h], iw + j0, iw + HALF + j0, sn, cs, n1, n2);
+        } else {
+#pragma unroll
+          for (int q = 0; q < kPairs; ++q) { n1[q] = make_float2(0.f, 0.f); n2[q] = n1[q]; }
+        }
+        dsum = row_sum<L>(bwd_lane_reduce_n(n1, n2, g1, g2, e, t == 0, w + j0, w + HALF + j0, sn, cs,
+                                            acc1p, acc2p, dnw1, dnw2));
+      } else {
+        r = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
+        dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, r, e, t == 0, w + j0, w + HALF + j0, sn,
+                                          cs, acc1p, acc2p, dnw1, dnw2));
+      }
       if (t == 0) {
         // d scales: the row's sum(dn w n), reduced over the warp's position slots.
         float v = dsum;
@@ -115,7 +141,10 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
       }
       if (!ok) continue;
       Chunk<T> out1, out2;
-      bwd_lane_dx(x1, x2, r, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
+      if constexpr (INV)
+        bwd_lane_dx_n<T>(n1, n2, r, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
+      else
+        bwd_lane_dx(x1, x2, r, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
       T* dp = db + b * sd.b + (int64_t)h * sd.h + n * sd.n + j0;
       store_stream<T, VEC>(dp, out1);
       store_stream<T, VEC>(dp + HALF, out2);
@@ -184,8 +213,8 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_finalize_kernel(
   }
 }
 
-size_t bwd_smem_bytes(int H, int D) {
-  return (size_t)(2 * D + H + kWarps * H + kWarps * D) * sizeof(float);
+size_t bwd_smem_bytes(int H, int D, bool inv) {
+  return (size_t)(2 * D + H + kWarps * H + kWarps * D + (inv ? 2 * D + H : 0)) * sizeof(float);
 }
 
 // Grid for the backward kernel: persistent, and even whenever it is smaller
@@ -196,18 +225,19 @@ static int64_t even_grid(int64_t grid, int64_t n_items) {
 }
 
 template <typename T, int D, bool VEC>
-static const void* bwd_kernel_ptr() {
-  return reinterpret_cast<const void*>(&prologue_bwd_kernel<T, D, VEC>);
+static const void* bwd_kernel_ptr(bool inv) {
+  return inv ? reinterpret_cast<const void*>(&prologue_bwd_kernel<T, D, VEC, true>)
+             : reinterpret_cast<const void*>(&prologue_bwd_kernel<T, D, VEC, false>);
 }
 
-static const void* bwd_kernel_for(int dtype, int D, bool vec) {
-#define FP_BWD_CASE(T)                                                              \
-  switch (D) {                                                                      \
-    case 32: return vec ? bwd_kernel_ptr<T, 32, true>() : bwd_kernel_ptr<T, 32, false>();   \
-    case 64: return vec ? bwd_kernel_ptr<T, 64, true>() : bwd_kernel_ptr<T, 64, false>();   \
-    case 128: return vec ? bwd_kernel_ptr<T, 128, true>() : bwd_kernel_ptr<T, 128, false>(); \
-    case 256: return vec ? bwd_kernel_ptr<T, 256, true>() : bwd_kernel_ptr<T, 256, false>(); \
-    default: return nullptr;                                                        \
+static const void* bwd_kernel_for(int dtype, int D, bool vec, bool inv) {
+#define FP_BWD_CASE(T)                                                                       \
+  switch (D) {                                                                               \
+    case 32: return vec ? bwd_kernel_ptr<T, 32, true>(inv) : bwd_kernel_ptr<T, 32, false>(inv);    \
+    case 64: return vec ? bwd_kernel_ptr<T, 64, true>(inv) : bwd_kernel_ptr<T, 64, false>(inv);    \
+    case 128: return vec ? bwd_kernel_ptr<T, 128, true>(inv) : bwd_kernel_ptr<T, 128, false>(inv); \
+    case 256: return vec ? bwd_kernel_ptr<T, 256, true>(inv) : bwd_kernel_ptr<T, 256, false>(inv); \
+    default: return nullptr;                                                                 \
   }
   switch (dtype) {
     case 0: FP_BWD_CASE(__nv_bfloat16)
@@ -218,18 +248,18 @@ static const void* bwd_kernel_for(int dtype, int D, bool vec) {
 #undef FP_BWD_CASE
 }
 
-int64_t bwd_grid(const Geometry& g, int H, int D, int dtype, bool vec) {
-  const void* fn = bwd_kernel_for(dtype, D, vec);
+int64_t bwd_grid(const Geometry& g, int H, int D, int dtype, bool vec, bool inv) {
+  const void* fn = bwd_kernel_for(dtype, D, vec, inv);
   if (!fn) return -1;
-  const int64_t grid = persistent_grid(fn, bwd_smem_bytes(H, D), g.n_items);
+  const int64_t grid = persistent_grid(fn, bwd_smem_bytes(H, D, inv), g.n_items);
   return grid > 0 ? even_grid(grid, g.n_items) : grid;
 }
 
 cudaError_t launch_bwd(const BwdArgs& a, float* dw, float* ds, int dtype, int D, bool vec,
-                       cudaStream_t stream) {
-  const void* fn = bwd_kernel_for(dtype, D, vec);
+                       bool inv, cudaStream_t stream) {
+  const void* fn = bwd_kernel_for(dtype, D, vec, inv);
   if (!fn) return cudaErrorInvalidValue;
-  const size_t smem = bwd_smem_bytes(a.H, D);
+  const size_t smem = bwd_smem_bytes(a.H, D, inv);
   int64_t grid = persistent_grid(fn, smem, a.g.n_items);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
   grid = even_grid(grid, a.g.n_items);

@@ -6,6 +6,8 @@
 // Q * exp(scale); .to(dtype)) operation by operation, with every product and sum
 // rounded separately (no FMA contraction) so the FP32 intermediates round like
 // the eager formulation; only the order of the D-element sum of squares differs.
+// Optionally the kernel also stores r = 1/sqrt(mean(x^2)+eps) of every row (the
+// saved statistic of the inverse formulation, fused_epilogue.py:1916-1917).
 #include "prologue_host.h"
 
 namespace flash_prologue {
@@ -63,6 +65,7 @@ __global__ void __launch_bounds__(kThreads) prologue_fwd_kernel(const FwdArgs a)
       const float ss = row_sum<L>(lane_sumsq(x1, x2));
       if (!ok) continue;  // after the shuffles: every lane took part in them
       const float r = inv_rms<D>(ss, a.eps);
+      if (a.rms[t] != nullptr && c == 0) a.rms[t][(b * a.H + h) * a.N + n] = r;
       Chunk<T> out1, out2;
       fwd_lane(x1, x2, r, w + j0, w + HALF + j0, sn, cs, t == 0, t == 0 ? e_s[h] : 1.f, out1, out2);
       T* yp = yb + b * sy.b + (int64_t)h * sy.h + n * sy.n + j0;

@@ -19,6 +19,7 @@ struct FwdArgs {
   const float* sin;
   const float* cos;
   TableStrides ssin, scos;
+  float* rms[2];        // optional: r = 1/sqrt(mean(x^2)+eps) per row, FP32 [B, H, N]
   int64_t B, N;
   int H;
   float eps;
@@ -36,6 +37,9 @@ struct BwdArgs {
   const float* cos;
   TableStrides ssin, scos;
   float* partials;  // [grid, 2*D + H] per-CTA partial sums
+  // Inverse backward only: x[] are the forward OUTPUTS and rms[] their saved
+  // r per row (FP32 [B, H, N]); the normalised rows are rebuilt from them.
+  const float* rms[2];
   int64_t B, N;
   int H;
   float eps;
@@ -74,6 +78,7 @@ struct TmaFwdArgs {
   const float* sin;
   const float* cos;
   int64_t sin_b, cos_b;  // batch strides of the tables; their n stride is D/2
+  float* rms[2];         // optional: r per row, FP32 [B, H, N]
   int64_t B, N;
   int H;
   float eps;
@@ -90,6 +95,7 @@ struct TmaBwdArgs {
   const float* cos;
   int64_t sin_b, cos_b;
   float* partials;      // [grid, 2*D + H]
+  const float* rms[2];  // inverse backward: saved r per row (in[] hold q_out, k_out)
   int64_t B, N;
   int H;
   float eps;
@@ -97,15 +103,15 @@ struct TmaBwdArgs {
 };
 
 TmaPlan plan_tma(int64_t B, int64_t H, int64_t N, int D, int dtype, bool heads_inner, int stages);
-size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H);
+size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv = false);
 // Read (synchronously) and optionally clear the error words of the bulk-copy
 // prologue kernels and of the fused QKV GEMM.
 cudaError_t read_device_error(int* value, bool reset);
 cudaError_t read_gemm_device_error(int* value, bool reset);
-int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype);
+int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype, bool inv = false);
 cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream);
 cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype, int D,
-                           cudaStream_t stream);
+                           bool inv, cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // Geometry of a problem (layout-dependent, device-independent).
@@ -123,9 +129,10 @@ cudaError_t launch_bwd_finalize(const float* partials, int64_t G, int C, int two
 cudaError_t launch_fwd(const FwdArgs& a, int dtype, int D, bool vec, cudaStream_t stream);
 
 // Grid the backward kernel uses for this geometry on the current device.
-int64_t bwd_grid(const Geometry& g, int H, int D, int dtype, bool vec);
-size_t bwd_smem_bytes(int H, int D);
+// `inv` selects the inverse backward (rows rebuilt from outputs and saved r).
+int64_t bwd_grid(const Geometry& g, int H, int D, int dtype, bool vec, bool inv = false);
+size_t bwd_smem_bytes(int H, int D, bool inv = false);
 cudaError_t launch_bwd(const BwdArgs& a, float* dw, float* ds, int dtype, int D, bool vec,
-                       cudaStream_t stream);
+                       bool inv, cudaStream_t stream);
 
 }  // namespace flash_prologue

@@ -214,6 +214,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       lds_f8(sn, sin_s + (p_l * HALF + j0) * 4);
       lds_f8(cs, cos_s + (p_l * HALF + j0) * 4);
       const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
+      if (a.rms[t] != nullptr && c == 0) {
+        const int64_t n = a.p.heads_inner ? (int64_t)tc.o0 + o_l : (int64_t)tc.i0 + i_l;
+        a.rms[t][((int64_t)tc.b * a.H + h) * a.N + n] = rr;
+      }
       Chunk<T> out1, out2;
       fwd_lane(x1, x2, rr, wa, wb, sn, cs, t == 0, t == 0 ? e_s[h] : 1.f, out1, out2);
       T* yp = ytile + (int64_t)i_l * so_inner + (int64_t)o_l * so_outer;
@@ -226,8 +230,19 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
 }
 
 // ---------------------------------------------------------------------------
-// Backward
-template <typename T, int D>
+// Backward. INV = true is the inverse backward: the streamed "inputs" are the
+// forward outputs, and each row's saved r is read from a.rms (prefetched
+// before the stage's barrier wait so its latency overlaps the copy).
+__device__ __forceinline__ float load_saved_r(const TmaBwdArgs& a, const TileCoords& tc, int t, int r) {
+  const int o_l = r >> a.p.log2_ti;
+  const int i_l = r & (a.p.ti - 1);
+  if (o_l >= tc.vo || i_l >= tc.vi) return 0.f;
+  const int64_t h = a.p.heads_inner ? (int64_t)tc.i0 + i_l : (int64_t)tc.o0 + o_l;
+  const int64_t n = a.p.heads_inner ? (int64_t)tc.o0 + o_l : (int64_t)tc.i0 + i_l;
+  return __ldg(a.rms[t] + ((int64_t)tc.b * a.H + h) * a.N + n);
+}
+
+template <typename T, int D, bool INV>
 __global__ void __launch_bounds__(kTmaThreads, 2)
     prologue_bwd_tma_kernel(const __grid_constant__ TmaBwdArgs a) {
   using S_ = TmaShape<T, D>;
@@ -244,6 +259,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   float* e_s = w_s + 2 * D;                            // [H]
   float* ds_s = e_s + a.H;                             // [4][H]  (Q warps)
   float* dw_s = ds_s + 4 * a.H;                        // [8][D]
+  float* iw_s = dw_s + 8 * D;                          // INV: [2 * D] 1 / w
+  float* ie_s = iw_s + 2 * D;                          // INV: [H] 1 / exp(scales)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -255,6 +272,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   for (int i = threadIdx.x; i < 2 * D; i += kTmaThreads) w_s[i] = a.w[i];
   for (int i = threadIdx.x; i < a.H; i += kTmaThreads) e_s[i] = (float)exp((double)a.scales[i]);
   for (int i = threadIdx.x; i < 4 * a.H; i += kTmaThreads) ds_s[i] = 0.f;
+  if constexpr (INV) {
+    for (int i = threadIdx.x; i < 2 * D; i += kTmaThreads) iw_s[i] = __frcp_rn(a.w[i]);
+    for (int i = threadIdx.x; i < a.H; i += kTmaThreads) ie_s[i] = (float)(1.0 / exp((double)a.scales[i]));
+  }
   __syncthreads();
 
   const int warp = threadIdx.x >> 5;
@@ -285,6 +306,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   const int j0 = c * kChunk;
   const float* wa = w_s + t * D + j0;
   const float* wb = wa + HALF;
+  const float* iwa = iw_s + t * D + j0;
+  const float* iwb = iwa + HALF;
   T* db = static_cast<T*>(a.dx[t]);
   const RowStrides sd = a.sd[t];
   const int64_t sd_inner = a.p.heads_inner ? sd.h : sd.n;
@@ -307,11 +330,17 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
 #pragma unroll
   for (int q = 0; q < kPairs; ++q) { acc1p[q] = make_float2(0.f, 0.f); acc2p[q] = make_float2(0.f, 0.f); }
 
+  static_assert(S_::PASSES <= 2, "saved-r prefetch holds two rows per thread");
   int k = 0;
   for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {
     const int s = k % S;
-    if (!mbar_wait(&full[s], (k / S) & 1)) break;
     const TileCoords tc = tile_coords(a.p, cur);
+    float rv0 = 0.f, rv1 = 0.f;  // INV: saved r of this thread's rows in passes 0 and 1
+    if constexpr (INV) {
+      rv0 = load_saved_r(a, tc, t, slot);
+      if (S_::PASSES > 1) rv1 = load_saved_r(a, tc, t, S_::ROWS_PER_PASS + slot);
+    }
+    if (!mbar_wait(&full[s], (k / S) & 1)) break;
     const unsigned char* st = smem + s * stage_bytes;
     const unsigned char* tile_x = st + (2 * t) * kTmaTileBytes;
     const unsigned char* tile_g = st + (2 * t + 1) * kTmaTileBytes;
@@ -344,10 +373,24 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       }
       const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
-      const float rr = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
       float2 dnw1[kPairs], dnw2[kPairs];
-      const float dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, rr, e, t == 0, wa, wb, sn, cs,
-                                                    acc1p, acc2p, dnw1, dnw2));
+      float2 n1[kPairs], n2[kPairs];  // INV: the rebuilt normalised row
+      float rr, dsum;
+      if constexpr (INV) {
+        rr = pass == 0 ? rv0 : rv1;
+        if (ok) {
+          inv_lane_normed(x1, x2, t == 0, ie_s[h], iwa, iwb, sn, cs, n1, n2);
+        } else {
+#pragma unroll
+          for (int q = 0; q < kPairs; ++q) { n1[q] = make_float2(0.f, 0.f); n2[q] = n1[q]; }
+        }
+        dsum = row_sum<L>(bwd_lane_reduce_n(n1, n2, g1, g2, e, t == 0, wa, wb, sn, cs, acc1p, acc2p,
+                                            dnw1, dnw2));
+      } else {
+        rr = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
+        dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, rr, e, t == 0, wa, wb, sn, cs, acc1p,
+                                          acc2p, dnw1, dnw2));
+      }
       if (t == 0) {
         float v = dsum;
         for (int bit = ps_lo; bit < ps_hi; ++bit)
@@ -356,7 +399,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       }
       if (!ok) continue;
       Chunk<T> out1, out2;
-      bwd_lane_dx(x1, x2, rr, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
+      if constexpr (INV)
+        bwd_lane_dx_n<T>(n1, n2, rr, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
+      else
+        bwd_lane_dx(x1, x2, rr, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
       T* dp = dtile + (int64_t)i_l * sd_inner + (int64_t)o_l * sd_outer;
       store_stream<T, true>(dp, out1);
       store_stream<T, true>(dp + HALF, out2);
@@ -414,27 +460,31 @@ cudaError_t read_device_error(int* value, bool reset) {
   return cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
 }
 
-size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H) {
+size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv) {
   const size_t table = (size_t)p.P * (D / 2) * 4;
   const size_t stage = (size_t)n_tensors * kTmaTileBytes + 2 * table;
   size_t extra = (size_t)2 * p.stages * sizeof(uint64_t) + (size_t)(2 * D + H) * 4;
   if (n_tensors == 4) extra += (size_t)(4 * H + 8 * D) * 4;
+  if (inv) extra += (size_t)(2 * D + H) * 4;
   return p.stages * stage + extra;
 }
 
 template <typename T, int D>
 static const void* fwd_tma_ptr() { return reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D>); }
 template <typename T, int D>
-static const void* bwd_tma_ptr() { return reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D>); }
+static const void* bwd_tma_ptr(bool inv) {
+  return inv ? reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, true>)
+             : reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, false>);
+}
 
-static const void* tma_kernel_for(bool bwd, int dtype, int D) {
-#define FP_TMA_CASE(T)                                                    \
-  switch (D) {                                                            \
-    case 32: return bwd ? bwd_tma_ptr<T, 32>() : fwd_tma_ptr<T, 32>();     \
-    case 64: return bwd ? bwd_tma_ptr<T, 64>() : fwd_tma_ptr<T, 64>();     \
-    case 128: return bwd ? bwd_tma_ptr<T, 128>() : fwd_tma_ptr<T, 128>();  \
-    case 256: return bwd ? bwd_tma_ptr<T, 256>() : fwd_tma_ptr<T, 256>();  \
-    default: return nullptr;                                              \
+static const void* tma_kernel_for(bool bwd, int dtype, int D, bool inv) {
+#define FP_TMA_CASE(T)                                                       \
+  switch (D) {                                                               \
+    case 32: return bwd ? bwd_tma_ptr<T, 32>(inv) : fwd_tma_ptr<T, 32>();     \
+    case 64: return bwd ? bwd_tma_ptr<T, 64>(inv) : fwd_tma_ptr<T, 64>();     \
+    case 128: return bwd ? bwd_tma_ptr<T, 128>(inv) : fwd_tma_ptr<T, 128>();  \
+    case 256: return bwd ? bwd_tma_ptr<T, 256>(inv) : fwd_tma_ptr<T, 256>();  \
+    default: return nullptr;                                                 \
   }
   switch (dtype) {
     case 0: FP_TMA_CASE(__nv_bfloat16)
@@ -450,16 +500,16 @@ static cudaError_t prepare_kernel(const void* fn, size_t smem) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 
-int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype) {
-  const void* fn = tma_kernel_for(bwd, dtype, D);
+int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype, bool inv) {
+  const void* fn = tma_kernel_for(bwd, dtype, D, inv);
   if (!fn) return -1;
-  const size_t smem = tma_smem_bytes(p, D, bwd ? 4 : 2, H);
+  const size_t smem = tma_smem_bytes(p, D, bwd ? 4 : 2, H, inv);
   if (prepare_kernel(fn, smem) != cudaSuccess) return -1;
   return persistent_grid(fn, smem, p.n_tiles, kTmaThreads);
 }
 
 cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream) {
-  const void* fn = tma_kernel_for(false, dtype, D);
+  const void* fn = tma_kernel_for(false, dtype, D, false);
   if (!fn) return cudaErrorInvalidValue;
   const size_t smem = tma_smem_bytes(a.p, D, 2, a.H);
   cudaError_t err = prepare_kernel(fn, smem);
@@ -473,10 +523,10 @@ cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t s
 }
 
 cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype, int D,
-                           cudaStream_t stream) {
-  const void* fn = tma_kernel_for(true, dtype, D);
+                           bool inv, cudaStream_t stream) {
+  const void* fn = tma_kernel_for(true, dtype, D, inv);
   if (!fn) return cudaErrorInvalidValue;
-  const size_t smem = tma_smem_bytes(a.p, D, 4, a.H);
+  const size_t smem = tma_smem_bytes(a.p, D, 4, a.H, inv);
   cudaError_t err = prepare_kernel(fn, smem);
   if (err != cudaSuccess) return err;
   const int64_t grid = persistent_grid(fn, smem, a.p.n_tiles, kTmaThreads);

@@ -6,7 +6,9 @@ Registers, under the reference's names and schemas:
   flash_attn_prologue/fused_epilogue.py:702-815, fake :817-828);
 * ``flash_prologue::qknorm_rope_scale_cute_backward`` (reference:
   fused_epilogue.py:1304-1423, fake :1425-1437);
-* the autograd link between them (reference: fused_epilogue.py:1440-1458).
+* the autograd link between them (reference: fused_epilogue.py:1440-1458);
+* ``flash_prologue::qknorm_rope_scale_cute_inverse`` / ``_inverse_backward``
+  and their autograd link (reference: fused_epilogue.py:2560-2805).
 
 Raw-op contract kept from the reference: q/k are 4-D ``[B, H, N, D]`` views
 with channel stride 1 and no expanded (stride-0) dimension, rejected with the
@@ -85,9 +87,12 @@ def _check_common(q, k, rmsnorm_weight, scales, sin, cos, eps):
         raise ValueError("eps must be finite and positive")
     if tuple(rmsnorm_weight.shape) != (2, 1, d) or scales.numel() != h:
         raise ValueError("weight must be [2,1,D], log-scales must be [H,1,1]")
+    # Like the reference's raw ops, which read these as Float32 whatever their
+    # dtype, any floating dtype is accepted and converted to FP32 (the public
+    # frontend still requires FP32, as the reference's does).
     for value in (rmsnorm_weight, scales, sin, cos):
-        if value.dtype != torch.float32:
-            raise ValueError("weights, log-scales, and sin/cos must be FP32")
+        if not value.dtype.is_floating_point:
+            raise ValueError("weights, log-scales, and sin/cos must be floating point")
     for t in (k, rmsnorm_weight, scales, sin, cos):
         if t.device != q.device:
             raise ValueError("all tensors must share a device")
@@ -98,6 +103,8 @@ def _check_common(q, k, rmsnorm_weight, scales, sin, cos, eps):
 def _table(t: torch.Tensor, B: int, N: int, half: int):
     """(b, n, j) element strides of a sin/cos table broadcast to [B, 1, N, D/2]."""
     t4 = _ensure_4d(t)
+    if t4.dtype != torch.float32:
+        t4 = t4.float()
     if t4.ndim != 4 or t4.shape[1] != 1 or t4.shape[3] != half:
         raise ValueError("sin/cos must broadcast over [B,1,N,D/2]")
     if t4.shape[0] not in (1, B) or t4.shape[2] not in (1, N):
@@ -146,8 +153,8 @@ def qknorm_rope_scale_cute_op(
         return q_out, k_out
     sin4, sin_str = _table(sin, B, N, D // 2)
     cos4, cos_str = _table(cos, B, N, D // 2)
-    w = rmsnorm_weight.contiguous()
-    s = scales.contiguous()
+    w = rmsnorm_weight.float().contiguous()
+    s = scales.float().contiguous()
     lib = _lib.load()
     with _DeviceGuard(q.device):
         status = lib.flash_prologue_fwd(
@@ -217,8 +224,8 @@ def qknorm_rope_scale_cute_backward_op(
     gk = _grad_view(grad_k_out, k)
     sin4, sin_str = _table(sin, B, N, D // 2)
     cos4, cos_str = _table(cos, B, N, D // 2)
-    w = rmsnorm_weight.contiguous()
-    s = scales.contiguous()
+    w = rmsnorm_weight.float().contiguous()
+    s = scales.float().contiguous()
     lib = _lib.load()
     with _DeviceGuard(q.device):
         nbytes = bwd_workspace_bytes(B, H, N, D, q.dtype) if q.numel() else 0
@@ -264,3 +271,156 @@ def _backward(ctx, grad_q, grad_k):
 
 torch.library.register_autograd("flash_prologue::qknorm_rope_scale_cute", _backward,
                                 setup_context=_setup_context)
+
+
+# ---------------------------------------------------------------------------
+# Inverse formulation: the forward also returns r = 1/sqrt(mean(x^2)+eps) per row,
+# and the backward rebuilds the normalised rows from the outputs and r, so a
+# training step need not keep q and k alive for the backward (the outputs are
+# kept for attention anyway). Reference: fused_epilogue.py:2560-2805.
+
+def _rms_shape_strides(q: torch.Tensor):
+    B, H, N = (int(x) for x in q.shape[:3])
+    return (B, H, N, 1), (H * N, N, 1, 1)
+
+
+@torch.library.custom_op("flash_prologue::qknorm_rope_scale_cute_inverse", mutates_args=())
+def qknorm_rope_scale_cute_inverse_op(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    rmsnorm_weight: torch.Tensor,
+    scales: torch.Tensor,
+    sin: torch.Tensor,
+    cos: torch.Tensor,
+    eps: float = 1e-5,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(q_out, k_out, rms_q, rms_k): the forward outputs and r per row, FP32 [B, H, N, 1]."""
+    _check_raw(q, k)
+    _check_common(q, k, rmsnorm_weight, scales, sin, cos, eps)
+    B, H, N, D = (int(x) for x in q.shape)
+    q_out = torch.empty_strided(q.shape, _get_compact_strides(q.shape, q.stride()),
+                                dtype=q.dtype, device=q.device)
+    k_out = torch.empty_strided(k.shape, _get_compact_strides(k.shape, k.stride()),
+                                dtype=k.dtype, device=k.device)
+    shape, strides = _rms_shape_strides(q)
+    rms_q = torch.empty_strided(shape, strides, dtype=torch.float32, device=q.device)
+    rms_k = torch.empty_strided(shape, strides, dtype=torch.float32, device=q.device)
+    if q.numel() == 0:
+        return q_out, k_out, rms_q, rms_k
+    sin4, sin_str = _table(sin, B, N, D // 2)
+    cos4, cos_str = _table(cos, B, N, D // 2)
+    w = rmsnorm_weight.float().contiguous()
+    s = scales.float().contiguous()
+    lib = _lib.load()
+    with _DeviceGuard(q.device):
+        status = lib.flash_prologue_inverse_fwd(
+            _lib.ptr(q), _lib.strides4(q), _lib.ptr(k), _lib.strides4(k),
+            _lib.ptr(q_out), _lib.strides4(q_out), _lib.ptr(k_out), _lib.strides4(k_out),
+            _lib.ptr(rms_q), _lib.ptr(rms_k), _lib.ptr(w), _lib.ptr(s),
+            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+            B, H, N, D, float(eps), _lib.DTYPE_CODES[q.dtype], _lib.stream_of(q.device))
+    _lib.check(status, "flash_prologue_inverse_fwd")
+    return q_out, k_out, rms_q, rms_k
+
+
+@qknorm_rope_scale_cute_inverse_op.register_fake
+def _qknorm_rope_scale_cute_inverse_fake(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5):
+    _check_raw(q, k)
+    shape, strides = _rms_shape_strides(q)
+    return (
+        torch.empty_strided(q.shape, _get_compact_strides(q.shape, q.stride()),
+                            dtype=q.dtype, device=q.device),
+        torch.empty_strided(k.shape, _get_compact_strides(k.shape, k.stride()),
+                            dtype=k.dtype, device=k.device),
+        torch.empty_strided(shape, strides, dtype=torch.float32, device=q.device),
+        torch.empty_strided(shape, strides, dtype=torch.float32, device=q.device),
+    )
+
+
+def _saved_rms(rms: torch.Tensor, q_out: torch.Tensor) -> torch.Tensor:
+    shape, _ = _rms_shape_strides(q_out)
+    if tuple(rms.shape) != shape or rms.dtype != torch.float32 or rms.device != q_out.device:
+        raise ValueError("rms_q/rms_k must be FP32 [B,H,N,1] on the activations' device")
+    return rms.contiguous()
+
+
+@torch.library.custom_op("flash_prologue::qknorm_rope_scale_cute_inverse_backward", mutates_args=())
+def qknorm_rope_scale_cute_inverse_backward_op(
+    q_out: torch.Tensor,
+    k_out: torch.Tensor,
+    rmsnorm_weight: torch.Tensor,
+    scales: torch.Tensor,
+    sin: torch.Tensor,
+    cos: torch.Tensor,
+    grad_q_out: torch.Tensor,
+    grad_k_out: torch.Tensor,
+    rms_q: torch.Tensor,
+    rms_k: torch.Tensor,
+    eps: float = 1e-5,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(dq, dk, dw, ds) from the forward outputs and the saved r (no q/k needed)."""
+    _check_raw(q_out, k_out)
+    _check_common(q_out, k_out, rmsnorm_weight, scales, sin, cos, eps)
+    B, H, N, D = (int(x) for x in q_out.shape)
+    grad_q = torch.empty_strided(q_out.shape, _get_compact_strides(q_out.shape, q_out.stride()),
+                                 dtype=q_out.dtype, device=q_out.device)
+    grad_k = torch.empty_strided(k_out.shape, _get_compact_strides(k_out.shape, k_out.stride()),
+                                 dtype=k_out.dtype, device=k_out.device)
+    grad_w = torch.empty((2, 1, D), dtype=torch.float32, device=q_out.device)
+    grad_s = torch.empty((H, 1, 1), dtype=torch.float32, device=q_out.device)
+    rq = _saved_rms(rms_q, q_out)
+    rk = _saved_rms(rms_k, q_out)
+    gq = _grad_view(grad_q_out, q_out)
+    gk = _grad_view(grad_k_out, k_out)
+    sin4, sin_str = _table(sin, B, N, D // 2)
+    cos4, cos_str = _table(cos, B, N, D // 2)
+    w = rmsnorm_weight.float().contiguous()
+    s = scales.float().contiguous()
+    lib = _lib.load()
+    with _DeviceGuard(q_out.device):
+        nbytes = bwd_workspace_bytes(B, H, N, D, q_out.dtype) if q_out.numel() else 0
+        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q_out.device)
+        status = lib.flash_prologue_inverse_bwd(
+            _lib.ptr(q_out), _lib.strides4(q_out), _lib.ptr(k_out), _lib.strides4(k_out),
+            _lib.ptr(rq), _lib.ptr(rk), _lib.ptr(w), _lib.ptr(s),
+            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+            _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
+            _lib.ptr(grad_q), _lib.strides4(grad_q), _lib.ptr(grad_k), _lib.strides4(grad_k),
+            _lib.ptr(grad_w), _lib.ptr(grad_s),
+            _lib.ptr(workspace), workspace.numel(),
+            B, H, N, D, float(eps), _lib.DTYPE_CODES[q_out.dtype], _lib.stream_of(q_out.device))
+    _lib.check(status, "flash_prologue_inverse_bwd")
+    return grad_q, grad_k, grad_w, grad_s
+
+
+@qknorm_rope_scale_cute_inverse_backward_op.register_fake
+def _qknorm_rope_scale_cute_inverse_backward_fake(q_out, k_out, rmsnorm_weight, scales, sin, cos,
+                                                  grad_q_out, grad_k_out, rms_q, rms_k, eps=1e-5):
+    _check_raw(q_out, k_out)
+    grad_q = torch.empty_strided(q_out.shape, _get_compact_strides(q_out.shape, q_out.stride()),
+                                 dtype=q_out.dtype, device=q_out.device)
+    grad_k = torch.empty_strided(k_out.shape, _get_compact_strides(k_out.shape, k_out.stride()),
+                                 dtype=k_out.dtype, device=k_out.device)
+    grad_w = torch.empty((2, 1, q_out.shape[-1]), device=q_out.device, dtype=torch.float32)
+    grad_s = torch.empty((q_out.shape[1], 1, 1), device=q_out.device, dtype=torch.float32)
+    return grad_q, grad_k, grad_w, grad_s
+
+
+def _inverse_setup_context(ctx, inputs, output):
+    q, k, rmsnorm_weight, scales, sin, cos, eps = inputs
+    q_out, k_out, rms_q, rms_k = output
+    ctx.save_for_backward(q_out, k_out, rmsnorm_weight, scales, sin, cos, rms_q, rms_k)
+    ctx.eps = eps
+
+
+def _inverse_backward(ctx, grad_q, grad_k, grad_rms_q, grad_rms_k):
+    # Like the reference (fused_epilogue.py:2791-2798), gradients that reach the
+    # saved statistics themselves are not propagated.
+    q_out, k_out, rmsnorm_weight, scales, sin, cos, rms_q, rms_k = ctx.saved_tensors
+    dq, dk, dw, ds = qknorm_rope_scale_cute_inverse_backward_op(
+        q_out, k_out, rmsnorm_weight, scales, sin, cos, grad_q, grad_k, rms_q, rms_k, ctx.eps)
+    return dq, dk, dw, ds, None, None, None
+
+
+torch.library.register_autograd("flash_prologue::qknorm_rope_scale_cute_inverse", _inverse_backward,
+                                setup_context=_inverse_setup_context)

@@ -128,6 +128,57 @@ FLASH_PROLOGUE_API int flash_prologue_bwd(const void* q, const int64_t q_strides
                        float eps, int dtype, void* stream);
 
 /*
+ * Inverse-formulation forward: flash_prologue_fwd, plus r = 1/sqrt(mean(x^2)+eps)
+ * of every row stored to rms_q / rms_k (FP32, contiguous [B, H, N], 4-byte
+ * aligned, both required). Saving r and the outputs lets the backward rebuild
+ * the normalised rows from the outputs instead of keeping q and k.
+ * Replaces flash_prologue::qknorm_rope_scale_cute_inverse
+ * (flash_attn_prologue/fused_epilogue.py:2560-2653) and its kernel
+ * (fused_epilogue.py:1663-1992), which stores the same statistic
+ * (fused_epilogue.py:1916-1917) but fixes eps at 1e-5; this entry point uses `eps`.
+ */
+FLASH_PROLOGUE_API int flash_prologue_inverse_fwd(const void* q, const int64_t q_strides[4],
+                       const void* k, const int64_t k_strides[4],
+                       void* q_out, const int64_t q_out_strides[4],
+                       void* k_out, const int64_t k_out_strides[4],
+                       float* rms_q, float* rms_k,
+                       const float* rmsnorm_weight, const float* scales,
+                       const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3],
+                       int64_t B, int64_t H, int64_t N, int64_t D,
+                       float eps, int dtype, void* stream);
+
+/*
+ * Inverse-formulation backward: the results of flash_prologue_bwd computed
+ * from the forward OUTPUTS q_out / k_out and the saved r (rms_q / rms_k, FP32
+ * contiguous [B, H, N]) instead of q / k. Per row the normalised values are
+ * rebuilt as n = R^T(out / exp(scale)) / w (R = the RoPE rotation; the Q scale
+ * only on Q), then dq/dk, d rmsnorm_weight and d scales follow as in the
+ * backward, with the same fixed-order reduction. Because the outputs were
+ * rounded to the activation dtype, the gradients differ from
+ * flash_prologue_bwd's by that rounding. `eps` is validated but unused (r is
+ * given); `workspace` as for flash_prologue_bwd, whose workspace size also
+ * covers this call.
+ * Replaces flash_prologue::qknorm_rope_scale_cute_inverse_backward
+ * (fused_epilogue.py:2671-2772) and its kernel (fused_epilogue.py:2067-2358),
+ * with the reference's float atomics replaced by the fixed-order reduction.
+ */
+FLASH_PROLOGUE_API int flash_prologue_inverse_bwd(const void* q_out, const int64_t q_out_strides[4],
+                       const void* k_out, const int64_t k_out_strides[4],
+                       const float* rms_q, const float* rms_k,
+                       const float* rmsnorm_weight, const float* scales,
+                       const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3],
+                       const void* grad_q_out, const int64_t gq_strides[4],
+                       const void* grad_k_out, const int64_t gk_strides[4],
+                       void* grad_q, const int64_t dq_strides[4],
+                       void* grad_k, const int64_t dk_strides[4],
+                       float* grad_rmsnorm_weight, float* grad_scales,
+                       void* workspace, size_t workspace_bytes,
+                       int64_t B, int64_t H, int64_t N, int64_t D,
+                       float eps, int dtype, void* stream);
+
+/*
  * Fused QKV projection GEMM with the prologue in its epilogue (tcgen05 tensor
  * cores, TMEM accumulators, TMA-fed). x: [M, K] BF16 row-major (M = B * S
  * tokens); w: [3*H*D, K] BF16 row-major (nn.Linear layout, rows Q | K | V

@@ -12,6 +12,10 @@ baseline. The product (``flash_attn_prologue_b200``) never imports it.
   and a closed-form backward following the identities of the reference's
   backward kernel (flash_attn_prologue/fused_epilogue.py:1047-1126).
 
+* ``inverse``: the reference's inverse (recompute-from-outputs) prologue
+  (flash_attn_prologue/fused_epilogue.py:2560-2805): forward = ``native`` plus
+  the per-row statistic r, backward restated op for op from the saved outputs.
+
 * ``compare``: the output bar -- 1 ulp, or within the FP32 rounding band of
   the rotation's term magnitudes where its two products nearly cancel.
 
@@ -22,3 +26,4 @@ checks both restatements against them.
 from .native import native_forward, native_forward_backward  # noqa: F401
 from .fp64 import fp64_forward, fp64_backward  # noqa: F401
 from .compare import check_outputs, term_magnitudes  # noqa: F401
+from .inverse import inverse_backward, inverse_forward  # noqa: F401
