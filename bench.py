@@ -385,7 +385,8 @@ def run_extras(device, steps=20):
     T, H, D = T_TOKENS, HEADS, HEAD_DIM
     buf = torch.randn(T, 3, H, D, generator=g, device=device).to(torch.bfloat16)
     q4, k4 = (buf[:, i].permute(1, 0, 2)[None] for i in (0, 1))
-    g4q, g4k = (torch.randn(1, H, T, D, generator=g, device=device).to(torch.bfloat16) for _ in range(2))
+    g4q, g4k = (torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16).permute(1, 0, 2)[None]
+                for _ in range(2))  # packed [T, H, D] upstream gradients, like the outputs
     sin, cos = rope_tables(torch.arange(T, device=device) % 4096, D, 10000.0)
     s4, c4 = sin[None, None], cos[None, None]
     w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)

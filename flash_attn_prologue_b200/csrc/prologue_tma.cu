@@ -127,8 +127,8 @@ __device__ __forceinline__ void lds_f8(float (&v)[kChunk], const unsigned char* 
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// Forward
-template <typename T, int D>
+// Forward. RMS = true also stores each row's r to a.rms (inverse formulation).
+template <typename T, int D, bool RMS>
 __global__ void __launch_bounds__(kTmaThreads, 2)
     prologue_fwd_tma_kernel(const __grid_constant__ TmaFwdArgs a) {
   using S_ = TmaShape<T, D>;
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       lds_f8(sn, sin_s + (p_l * HALF + j0) * 4);
       lds_f8(cs, cos_s + (p_l * HALF + j0) * 4);
       const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
-      if (a.rms[t] != nullptr && c == 0) {
+      if (RMS && c == 0) {
         const int64_t n = a.p.heads_inner ? (int64_t)tc.o0 + o_l : (int64_t)tc.i0 + i_l;
         a.rms[t][((int64_t)tc.b * a.H + h) * a.N + n] = rr;
       }
@@ -470,20 +470,24 @@ size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv) {
 }
 
 template <typename T, int D>
-static const void* fwd_tma_ptr() { return reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D>); }
+static const void* fwd_tma_ptr(bool rms) {
+  return rms ? reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, true>)
+             : reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, false>);
+}
 template <typename T, int D>
 static const void* bwd_tma_ptr(bool inv) {
   return inv ? reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, true>)
              : reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, false>);
 }
 
+// `inv`: the inverse backward, or for the forward the variant that stores r.
 static const void* tma_kernel_for(bool bwd, int dtype, int D, bool inv) {
 #define FP_TMA_CASE(T)                                                       \
   switch (D) {                                                               \
-    case 32: return bwd ? bwd_tma_ptr<T, 32>(inv) : fwd_tma_ptr<T, 32>();     \
-    case 64: return bwd ? bwd_tma_ptr<T, 64>(inv) : fwd_tma_ptr<T, 64>();     \
-    case 128: return bwd ? bwd_tma_ptr<T, 128>(inv) : fwd_tma_ptr<T, 128>();  \
-    case 256: return bwd ? bwd_tma_ptr<T, 256>(inv) : fwd_tma_ptr<T, 256>();  \
+    case 32: return bwd ? bwd_tma_ptr<T, 32>(inv) : fwd_tma_ptr<T, 32>(inv);     \
+    case 64: return bwd ? bwd_tma_ptr<T, 64>(inv) : fwd_tma_ptr<T, 64>(inv);     \
+    case 128: return bwd ? bwd_tma_ptr<T, 128>(inv) : fwd_tma_ptr<T, 128>(inv);  \
+    case 256: return bwd ? bwd_tma_ptr<T, 256>(inv) : fwd_tma_ptr<T, 256>(inv);  \
     default: return nullptr;                                                 \
   }
   switch (dtype) {
@@ -509,7 +513,7 @@ int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype, bool inv) 
 }
 
 cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream) {
-  const void* fn = tma_kernel_for(false, dtype, D, false);
+  const void* fn = tma_kernel_for(false, dtype, D, a.rms[0] != nullptr);
   if (!fn) return cudaErrorInvalidValue;
   const size_t smem = tma_smem_bytes(a.p, D, 2, a.H);
   cudaError_t err = prepare_kernel(fn, smem);

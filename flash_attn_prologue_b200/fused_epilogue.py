@@ -67,6 +67,8 @@ def _ensure_4d(t: torch.Tensor) -> torch.Tensor:
 
 
 def _check_raw(q: torch.Tensor, k: torch.Tensor) -> None:
+    if q.numel() == 0 and k.numel() == 0:
+        return  # no elements: any strides (compact strides of empty tensors hold zeros)
     if any(n > 1 and st == 0 for t in (q, k) for n, st in zip(t.shape, t.stride())):
         raise ValueError(_EXPANDED_MSG)
     if q.stride(-1) != 1 or k.stride(-1) != 1:
