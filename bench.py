@@ -407,20 +407,39 @@ def run_extras(device, steps=20):
     w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
     s = 0.1 * torch.randn(H, 1, 1, generator=g, device=device)
     flop = 2 * T * 3 * H * D * hidden
-    fused_ms = _event_ms(lambda: fap.fused_qkv_epilogue(x, wq, w, s, sin, cos), steps)
+
+    def fused():
+        return fap.fused_qkv_epilogue(x, wq, w, s, sin, cos)
+
+    def gemm_only():
+        return fap.fused_qkv(x, wq)
 
     def unfused():
         p = torch.nn.functional.linear(x[0], wq).view(T, 3, H, D)
         return qknorm_rope_scale(p[:, 0], p[:, 1], w, s, sin, cos, backend="cute")
-    unfused_ms = _event_ms(unfused, steps)
-    linear_ms = _event_ms(lambda: torch.nn.functional.linear(x[0], wq), steps)
-    tf = flop / (fused_ms * 1e-3) / 1e12
-    out["c5_fused_qkv_gemm"] = {
-        "ms": round(fused_ms, 4), "tflops": round(tf, 1), "frac_of_measured_bf16": round(tf / bf16_peak, 4),
-        "bf16_peak_tflops": bf16_peak, "flop": flop,
-        "cublas_linear_then_prologue_kernel_ms": round(unfused_ms, 4),
-        "cublas_linear_alone_ms": round(linear_ms, 4),
-        "note": "fused = one tcgen05 kernel writing Q,K (prologue applied), V and the BF16 Q/K projections"}
+
+    def linear():
+        return torch.nn.functional.linear(x[0], wq)
+
+    sustained_sm = _measured("bf16_tflops_sustained", 1410.0)
+    c5 = {"bf16_peak_tflops": bf16_peak, "bf16_sustained_peak_tflops": sustained_sm, "flop": flop}
+    # Burst: `steps` launches; sustained: ~0.6 s of back-to-back launches, where
+    # the 1 kW power cap sets the clocks (the regime of a long training run).
+    for regime, n in (("burst", steps), ("sustained", 450)):
+        ms = {name: _event_ms(fn, n) for name, fn in
+              (("fused", fused), ("gemm_only", gemm_only), ("cublas_linear_then_prologue_kernel", unfused),
+               ("cublas_linear_alone", linear))}
+        peak_ref = bf16_peak if regime == "burst" else sustained_sm
+        tf = flop / (ms["fused"] * 1e-3) / 1e12
+        c5[regime] = {"launches": n, "tflops": round(tf, 1), "frac_of_measured_bf16": round(tf / peak_ref, 4),
+                      **{f"{k}_ms": round(v, 4) for k, v in ms.items()}}
+    c5["ms"] = c5["burst"]["fused_ms"]
+    c5["tflops"] = c5["burst"]["tflops"]
+    c5["frac_of_measured_bf16"] = c5["burst"]["frac_of_measured_bf16"]
+    c5["note"] = ("fused = one tcgen05 kernel (2-CTA clusters, cta_group::2) writing Q,K (prologue applied), "
+                  "V and the BF16 Q/K projections; gemm_only = the same kernel without the prologue; "
+                  "burst fractions against bf16_tflops, sustained against bf16_tflops_sustained")
+    out["c5_fused_qkv_gemm"] = c5
     return out
 
 

@@ -54,6 +54,7 @@ SIGNATURES = {
                                      _vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _vp, _vp,
                                      ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
     "flash_prologue_set_path": ([ctypes.c_int], ctypes.c_int),
+    "flash_prologue_set_gemm_variant": ([ctypes.c_int], ctypes.c_int),
     "flash_prologue_device_error": ([ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
     "flash_prologue_bwd": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,
                             _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
@@ -93,6 +94,11 @@ def load():
 def set_path(mode: int) -> None:
     """0: bulk-copy pipeline when the layout allows (default); 1: register path only."""
     check(load().flash_prologue_set_path(int(mode)), "flash_prologue_set_path")
+
+
+def set_gemm_variant(variant: int) -> None:
+    """Fused QKV GEMM mainloop: 0 = CTA pairs (default), 1 = one CTA per SM."""
+    check(load().flash_prologue_set_gemm_variant(int(variant)), "flash_prologue_set_gemm_variant")
 
 
 def device_error(reset: bool = True) -> int:

@@ -10,20 +10,30 @@
 // the reference's GEMM launch + two copies + in-place prologue launch
 // (flash_attn_prologue/fused_qkv.py:698-825) with one kernel.
 //
-// Structure (one persistent CTA per SM, 6 warps):
-//   warp 4      TMA producer: 128x64 X tiles and 256x64 W tiles, 128-byte
-//               swizzled, into a 4-stage shared-memory ring (full/empty mbarriers);
-//   warp 5      allocates 512 TMEM columns; one thread issues tcgen05.mma
-//               (M=128, N=256, K=16, BF16 -> FP32) into one of two TMEM
-//               accumulators and commits stage releases / accumulator-ready;
-//   warps 0-3   epilogue: tcgen05.ld of the accumulator (thread = token row),
-//               BF16 rounding, sum of squares over the head, RoPE pairing of
-//               columns j and j + D/2 (both in the same thread), stores.
-// Double-buffered accumulators let the epilogue of tile i overlap the MMAs of
-// tile i + 1. Tiles are ordered with the N tile fastest, so CTAs working at the
-// same time share X rows through L2 (W stays L2-resident). All waits are
-// bounded (tma_util.cuh); a timeout records an error, and TMEM is released on
-// every path.
+// Two mainloops share one epilogue:
+//
+// * CTA pair (default): 2-CTA clusters, one persistent pair per two SMs. A
+//   tile is 256 tokens x 256 output columns. Each CTA's warp 4 loads its own
+//   halves -- X rows [m0 + 128*rank, +128) and W rows [n0 + 128*rank, +128),
+//   64 columns of K per stage, 128-byte swizzled -- into a 5-stage ring; all
+//   four loads of a stage count their bytes on the even CTA's full barrier.
+//   One thread of the even CTA issues tcgen05.mma.cta_group::2 (M = 256,
+//   N = 256, K = 16): the tensor cores of both SMs read A from their own
+//   shared memory and B from both, and each CTA's tensor memory receives its
+//   128 rows. Per SM this moves 32 KB of operands per 128x256x64 of work
+//   instead of 48 KB, which is what limits the single-CTA loop.
+// * Single CTA: one persistent CTA per SM, 128 x 256 tiles, 4-stage ring of
+//   48 KB stages, tcgen05.mma.cta_group::1 (M = 128).
+//
+// In both, warp 5 owns the 512 tensor-memory columns (two 256-column FP32
+// accumulators, so tile i's epilogue overlaps tile i+1's MMAs) and warps 0-3
+// are the epilogue: tcgen05.ld of the accumulator (TMEM lane = token row),
+// BF16 rounding, sum of squares over the head, RoPE pairing of columns j and
+// j + D/2 (both in the same thread), stores through swizzled staging tiles and
+// TMA tensor stores. Tiles are ordered with the N tile fastest, so CTAs working
+// at the same time share X rows through L2 (W stays L2-resident). No load uses
+// cluster multicast. All waits are bounded (tma_util.cuh); a timeout records
+// an error, and tensor memory is released on every path.
 #include <cuda.h>
 
 #include "../../include/flash_prologue.h"
@@ -33,25 +43,49 @@
 namespace flash_prologue {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kStages = 4;
-constexpr int kStageA = BM * BK * 2;            // 16 KB
-constexpr int kStageB = BN * BK * 2;            // 32 KB
-constexpr int kStageBytes = kStageA + kStageB;  // 48 KB
+constexpr int BN = 256, BK = 64;
 constexpr int kAccCols = BN;                    // FP32 columns per accumulator
 constexpr int kTmemCols = 2 * kAccCols;         // two accumulators = all 512 columns
-constexpr int kEpiWarps = 4;
-constexpr int kProducerWarp = kEpiWarps;
-constexpr int kMmaWarp = kEpiWarps + 1;
-constexpr int kGemmThreads = (kEpiWarps + 2) * 32;
+// Warp roles: warps 0 .. EPI-1 epilogue, EPI the TMA producer, EPI+1 the
+// TMEM owner / MMA issuer.
+template <int EPI>
+struct Roles {
+  static constexpr int kEpi = EPI;
+  static constexpr int kProducer = EPI;
+  static constexpr int kMma = EPI + 1;
+  static constexpr int kThreads = (EPI + 2) * 32;
+};
 // Output staging: per epilogue warp, its 32 rows of one head as [32][128 B]
 // halves (64 BF16 columns each), 128-byte swizzled, written out by TMA stores.
 constexpr int kStageHalfBytes = 32 * 128;
 constexpr int kStagingPerWarp = 2 * kStageHalfBytes;  // up to D = 128
 
+// Single-CTA mainloop: 128 x 256 tiles, 4 epilogue warps.
+using RolesSingle = Roles<4>;
+constexpr int kRowsSingle = 128;
+constexpr int kStagesSingle = 4;
+constexpr int kStagingBufsSingle = 1;
+constexpr int kStageASingle = kRowsSingle * BK * 2;            // 16 KB
+constexpr int kStageBytesSingle = kStageASingle + BN * BK * 2;  // 48 KB
+
+// CTA-pair mainloop: 256 x 256 tiles, per CTA 128 rows of X and 128 of W.
+// Two configurations: with the prologue, 8 epilogue warps (two per SM
+// sub-partition, so one's latency hides under the other's work; 168 registers
+// a thread) and 5 stages; plain projection, 4 epilogue warps and 6 stages.
+constexpr int kRowsPair = 256;
+constexpr int kStagingBufsPair = 1;
+template <int EPI>
+struct PairConfig {
+  using R = Roles<EPI>;
+  static constexpr int kStages = EPI == 8 ? 5 : 6;
+  static constexpr int kSlots = 1;  // sin/cos ring slots
+};
+constexpr int kStageAPair = 128 * BK * 2;                         // 16 KB
+constexpr int kStageBytesPair = kStageAPair + (BN / 2) * BK * 2;  // 32 KB
+
 struct GemmArgs {
   int64_t M, K, H, D, S;          // S = tokens per batch (M = B * S)
-  int64_t n_tiles_n, n_tiles;
+  int64_t n_tiles_n, n_tiles;     // tiles of the mainloop in use (N tile fastest)
   const float* w;                 // RMSNorm weight [2, D]
   const float* scales;            // [H]
   const float* sin;
@@ -70,225 +104,165 @@ struct OutMaps {
   CUtensorMap m[5];
 };
 
-__device__ __forceinline__ float2 round_bf16_pair(uint32_t a, uint32_t b) {
-  return __bfloat1622float2(__floats2bfloat162_rn(__uint_as_float(a), __uint_as_float(b)));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float2 v) {
   __nv_bfloat162 p = __floats2bfloat162_rn(v.x, v.y);
   return *reinterpret_cast<uint32_t*>(&p);
 }
 
-// Stores 32 BF16 values (given as 16 packed words) as four 16-byte stores.
-__device__ __forceinline__ void store32(__nv_bfloat16* dst, const uint32_t (&p)[16]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) d[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
-}
-
-// Rounds one 32-column accumulator chunk to BF16 and stores it.
-__device__ __forceinline__ void store_chunk_rounded(__nv_bfloat16* dst, const uint32_t (&v)[32]) {
-  uint32_t p[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) p[i] = pack_bf16(round_bf16_pair(v[2 * i], v[2 * i + 1]));
-  store32(dst, p);
+// The two BF16 values of a packed pair as FP32 (exact).
+__device__ __forceinline__ float2 unpack_bf16(uint32_t p) {
+  return make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xFFFF0000u));
 }
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
+// Shared-memory carve-up common to both kernels: the operand ring (1024-byte
+// aligned), then the epilogue staging, barriers, the TMEM address slot and the
+// RMSNorm weight. Both CTAs of a pair get the same offsets.
+struct GemmSmem {
+  unsigned char* ring;
+  unsigned char* staging;  // [epilogue warps][NBUF][kStagingPerWarp]
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* acc_full;      // [2]
+  uint64_t* acc_empty;     // [2]
+  uint32_t* tmem_slot;
+  float* w_s;              // [2 * D]
+};
+
+template <int STAGES, int STAGE_BYTES, int NBUF, int EPI>
+__device__ __forceinline__ GemmSmem carve_smem(unsigned char* smem_raw) {
+  GemmSmem s;
+  s.ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                            ~uintptr_t(1023));
+  s.staging = s.ring + STAGES * STAGE_BYTES;
+  s.full = reinterpret_cast<uint64_t*>(s.staging + EPI * NBUF * kStagingPerWarp);
+  s.empty = s.full + STAGES;
+  s.acc_full = s.empty + STAGES;
+  s.acc_empty = s.acc_full + 2;
+  s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + 2);
+  s.w_s = reinterpret_cast<float*>(s.tmem_slot + 4);
+  return s;
+}
+
+constexpr size_t smem_bytes_for(int stages, int stage_bytes, int nbuf, int epi, int64_t D) {
+  return 1024 + (size_t)stages * stage_bytes + (size_t)epi * nbuf * kStagingPerWarp + 256 +
+         (size_t)(2 * D) * 4;
+}
+
 }  // namespace
 
-template <int D>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    qkv_gemm_prologue_kernel(const __grid_constant__ CUtensorMap tm_x,
-                             const __grid_constant__ CUtensorMap tm_w,
-                             const __grid_constant__ OutMaps om,
-                             const __grid_constant__ GemmArgs a) {
+// ---------------------------------------------------------------------------
+// Epilogue (warps 0 .. EPI-1). Processes the tiles tile0, tile0 + step, ...;
+// this CTA's accumulator rows are tokens (tile / n_tiles_n) * ROWS + m_off +
+// row. Warp w reads TMEM lanes 32 * (w % 4) .. + 31 (a warp may only access
+// its quarter of the lanes), so with EPI = 8 the warps w and w + 4 share rows
+// and split the heads of the tile between them. After reading an accumulator
+// each warp arrives once on acc_empty[buffer]: this CTA's barrier, or for a
+// pair the even CTA's, at the shared::cluster address acc_empty_cluster
+// (+ 8 bytes per buffer).
+template <int D, int ROWS, int NBUF, int EPI, int SLOTS>
+__device__ __forceinline__ void run_epilogue(const OutMaps& om, const GemmArgs& a, const GemmSmem& sm,
+                                             uint32_t tmem_base, int64_t tile0, int64_t step,
+                                             int m_off, uint32_t acc_empty_cluster) {
   constexpr int HALF = D / 2;
   constexpr int HEADS_PER_TILE = BN / D;
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* staging = smem + kStages * kStageBytes;  // [kEpiWarps][kStagingPerWarp]
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kEpiWarps * kStagingPerWarp);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
-  uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  float* w_s = reinterpret_cast<float*>(tmem_slot + 4);  // [2 * D]
-
+  constexpr int GROUPS = HALF / 16;     // 16-column groups of each half of a head
+  constexpr int HEAD_STEP = EPI / 4;    // warps sharing a lane quarter split the heads
+  static_assert(HEADS_PER_TILE % HEAD_STEP == 0, "heads per warp");
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+  const int quarter = warp & 3;
+  const int head0 = warp >> 2;
+  const int row = quarter * 32 + lane;  // TMEM lane == accumulator row
+  unsigned char* const stage_base = sm.staging + warp * NBUF * kStagingPerWarp;
+  unsigned char* stage_w = stage_base;  // the staging tile being filled
+  int cur = 0;
+  const bool staged = a.tma_store != 0;
+  // 16 output bytes (8 BF16 at column `col` of the head) of this thread's row:
+  // into the warp's swizzled staging tile, or straight to global memory.
+  auto emit16 = [&](__nv_bfloat16* grow, bool valid, int col, uint4 v) {
+    if (staged) {
+      unsigned char* half = stage_w + (col >> 6) * kStageHalfBytes;
+      const int chunk = (col & 63) >> 3;
+      *reinterpret_cast<uint4*>(half + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = v;
+    } else if (valid) {
+      *reinterpret_cast<uint4*>(grow + col) = v;
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpiWarps);
-    }
-    fence_mbar_init();
-  }
-  if (warp == kMmaWarp) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
-  }
-  if (a.apply_prologue) {
-    for (int i = threadIdx.x; i < 2 * D; i += kGemmThreads) w_s[i] = a.w[i];
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const int num_kb = (int)(a.K / BK);
-  bool failed = false;
-
-  if (warp == kProducerWarp) {
-    // ------------------------------ TMA producer ------------------------------
+  };
+  // Staged path: write the warp's 32 rows of one head to `map` at row0 (one
+  // bulk group) and move on to the next staging tile ...
+  auto flush = [&](const CUtensorMap* map, int64_t row0) {
+    fence_proxy_async_smem();
+    __syncwarp();
     if (lane == 0) {
-      prefetch_tmap(&tm_x);
-      prefetch_tmap(&tm_w);
-      uint32_t it = 0;
-      for (int64_t tile = blockIdx.x; tile < a.n_tiles && !failed; tile += gridDim.x) {
-        const int32_t m0 = (int32_t)((tile / a.n_tiles_n) * BM);
-        const int32_t n0 = (int32_t)((tile % a.n_tiles_n) * BN);
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
-          const int s = it % kStages;
-          if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1)) { failed = true; break; }
-          unsigned char* st = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&full[s], kStageBytes);
-          tma_load_2d(st, &tm_x, kb * BK, m0, &full[s]);
-          tma_load_2d(st + kStageA, &tm_w, kb * BK, n0, &full[s]);
-        }
-      }
+      for (int half = 0; half < D / 64; ++half)
+        tma_store_2d(map, half * 64, (int32_t)row0, stage_w + half * kStageHalfBytes);
+      bulk_commit_group();
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------ MMA issuer --------------------------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
-      uint32_t it = 0, tcount = 0;
-      for (int64_t tile = blockIdx.x; tile < a.n_tiles && !failed; tile += gridDim.x, ++tcount) {
-        const uint32_t abuf = tcount & 1;
-        if (!mbar_wait(&acc_empty[abuf], ((tcount >> 1) & 1) ^ 1)) { failed = true; break; }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + abuf * kAccCols;
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
-          const int s = it % kStages;
-          if (!mbar_wait(&full[s], (it / kStages) & 1)) { failed = true; break; }
-          tc_fence_after();
-          const uint32_t st = smem_u32(smem + s * kStageBytes);
-          const uint64_t adesc = smem_desc_k_sw128(st);
-          const uint64_t bdesc = smem_desc_k_sw128(st + kStageA);
+    cur = (cur + 1 == NBUF) ? 0 : cur + 1;
+    stage_w = stage_base + cur * kStagingPerWarp;
+  };
+  // ... and before filling a staging tile, wait until the stores issued from
+  // it (NBUF groups ago) have read it.
+  auto reclaim = [&]() {
+    if (lane == 0) bulk_wait_group_read<NBUF - 1>();
+    __syncwarp();
+  };
+  // The token's sin/cos values, 16 of each per group, in a ring of SLOTS group
+  // slots: the first SLOTS groups are requested before the accumulator wait
+  // (and again at the start of each further head when a head has more groups
+  // than slots), group g + SLOTS as soon as group g has been used.
+  static_assert(SLOTS >= 1 && SLOTS <= GROUPS, "sin/cos ring");
+  float sn[SLOTS][16], cs[SLOTS][16];
+  const float* srow = a.sin;
+  const float* crow = a.cos;
+  bool valid = false;
+  auto load_group = [&](int g, int slot) {
+    if (valid) {
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            // +32 bytes along K per step: +2 in the descriptor's start-address field.
-            umma_bf16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
-          }
-          umma_commit(&empty[s]);  // releases the stage once these MMAs have read it
-        }
-        if (failed) break;
-        umma_commit(&acc_full[abuf]);
+      for (int j = 0; j < 16; j += 4) {
+        const float4 s4 = ldg4(srow + 16 * g + j), c4 = ldg4(crow + 16 * g + j);
+        sn[slot][j] = s4.x; sn[slot][j + 1] = s4.y; sn[slot][j + 2] = s4.z; sn[slot][j + 3] = s4.w;
+        cs[slot][j] = c4.x; cs[slot][j + 1] = c4.y; cs[slot][j + 2] = c4.z; cs[slot][j + 3] = c4.w;
       }
-      // Wait for the last accumulator's MMAs before TMEM may be released.
-      if (tcount > 0 && !failed) {
-        const uint32_t last = tcount - 1;
-        mbar_wait(&acc_full[last & 1], (last >> 1) & 1);
-      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) { sn[slot][j] = 0.f; cs[slot][j] = 0.f; }
     }
-  } else {
-    // ------------------------------ epilogue ----------------------------------
-    const int row = warp * 32 + lane;  // TMEM lane == tile row
-    unsigned char* stage_w = staging + warp * kStagingPerWarp;
-    const bool staged = a.tma_store != 0;
-    // 16 output bytes (8 BF16 at column `col` of the head) of this thread's row:
-    // into the warp's swizzled staging tile, or straight to global memory.
-    auto emit16 = [&](__nv_bfloat16* grow, bool valid, int col, uint4 v) {
-      if (staged) {
-        unsigned char* half = stage_w + (col >> 6) * kStageHalfBytes;
-        const int chunk = (col & 63) >> 3;
-        *reinterpret_cast<uint4*>(half + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = v;
-      } else if (valid) {
-        *reinterpret_cast<uint4*>(grow + col) = v;
-      }
-    };
-    // Staged path: write the warp's 32 rows of one head to `map` at row0 ...
-    auto flush = [&](const CUtensorMap* map, int64_t row0) {
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        for (int half = 0; half < D / 64; ++half)
-          tma_store_2d(map, half * 64, (int32_t)row0, stage_w + half * kStageHalfBytes);
-        bulk_commit_group();
-      }
-    };
-    // ... and before refilling the staging tile, wait until those stores have read it.
-    auto reclaim = [&]() {
-      if (lane == 0) bulk_wait_group_read0();
-      __syncwarp();
-    };
-    // The token's sin/cos row (D/2 + D/2 floats), fetched for every Q/K tile
-    // before waiting for its accumulator so that the loads overlap the MMAs;
-    // every head of the tile shares it.
-    float sn[HALF], cs[HALF];
-    uint32_t tcount = 0;
-    for (int64_t tile = blockIdx.x; tile < a.n_tiles; tile += gridDim.x, ++tcount) {
-      const uint32_t abuf = tcount & 1;
-      const int64_t m = (tile / a.n_tiles_n) * BM + row;
-      const bool valid = m < a.M;
-      const int64_t b = m / a.S, sp = m % a.S;
-      // First token of this warp's 32 rows (S % 32 == 0 on the staged path,
-      // so all 32 share its batch index).
-      const int64_t mw = (tile / a.n_tiles_n) * BM + warp * 32;
-      const int64_t bw = mw / a.S, spw = mw % a.S;
-      const int64_t n0 = (tile % a.n_tiles_n) * BN;
-      const int seg = (int)(n0 / (a.H * D));  // the whole tile is Q (0), K (1) or V (2)
-      const bool prologue = a.apply_prologue && seg < 2;
-      if (prologue) {
-        if (valid) {
-          const float* srow = a.sin + b * a.sin_b + sp * a.sin_n;
-          const float* crow = a.cos + b * a.cos_b + sp * a.cos_n;
+  };
+  uint32_t tcount = 0;
+  for (int64_t tile = tile0; tile < a.n_tiles; tile += step, ++tcount) {
+    const uint32_t abuf = tcount & 1;
+    const int64_t mrow0 = (tile / a.n_tiles_n) * ROWS + m_off;
+    const int64_t m = mrow0 + row;
+    valid = m < a.M;
+    const int64_t b = m / a.S, sp = m % a.S;
+    // First token of this warp's 32 rows (S % 32 == 0 on the staged path,
+    // so all 32 share its batch index).
+    const int64_t mw = mrow0 + quarter * 32;
+    const int64_t bw = mw / a.S, spw = mw % a.S;
+    const int64_t n0 = (tile % a.n_tiles_n) * BN;
+    const int seg = (int)(n0 / (a.H * D));  // the whole tile is Q (0), K (1) or V (2)
+    const bool prologue = a.apply_prologue && seg < 2;
+    if (prologue) {
+      srow = a.sin + b * a.sin_b + sp * a.sin_n;
+      crow = a.cos + b * a.cos_b + sp * a.cos_n;
 #pragma unroll
-          for (int j = 0; j < HALF; j += 4) {
-            const float4 s4 = ldg4(srow + j), c4 = ldg4(crow + j);
-            sn[j] = s4.x; sn[j + 1] = s4.y; sn[j + 2] = s4.z; sn[j + 3] = s4.w;
-            cs[j] = c4.x; cs[j + 1] = c4.y; cs[j + 2] = c4.z; cs[j + 3] = c4.w;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < HALF; ++j) { sn[j] = 0.f; cs[j] = 0.f; }
-        }
-      }
-      if (!mbar_wait(&acc_full[abuf], (tcount >> 1) & 1)) break;
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + abuf * kAccCols + ((uint32_t)(warp * 32) << 16);
-      for (int hh = 0; hh < HEADS_PER_TILE; ++hh) {
-        const int h = (int)(((n0 + hh * D) % (a.H * D)) / D);
-        const uint32_t tcol = tbase + hh * D;
-        const int64_t out_off = ((b * a.H + h) * a.S + sp) * D;
-        const int64_t row0 = (bw * a.H + h) * a.S + spw;  // staged path: first output row
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out[seg]) + out_off;
-        if (staged) reclaim();
-        if (!prologue) {
+      for (int g = 0; g < SLOTS; ++g) load_group(g, g);
+    }
+    if (!mbar_wait(&sm.acc_full[abuf], (tcount >> 1) & 1)) break;
+    tc_fence_after();
+    const uint32_t tbase = tmem_base + abuf * kAccCols + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(tcol + 32 * c, v);
-            tmem_wait_ld();
-            uint32_t p[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) p[i] = pack_bf16(round_bf16_pair(v[2 * i], v[2 * i + 1]));
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              emit16(out, valid, 32 * c + 8 * q, make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]));
-          }
-          if (staged) flush(&om.m[seg], row0);
-          continue;
-        }
-        // Pass 1: BF16 projection, optional raw store, sum of squares.
-        const bool want_raw = a.raw[seg] != nullptr;
-        __nv_bfloat16* raw = want_raw ? static_cast<__nv_bfloat16*>(a.raw[seg]) + out_off : nullptr;
-        float2 acc = make_float2(0.f, 0.f);
+    for (int hh = head0; hh < HEADS_PER_TILE; hh += HEAD_STEP) {
+      const int h = (int)(((n0 + hh * D) % (a.H * D)) / D);
+      const uint32_t tcol = tbase + hh * D;
+      const int64_t out_off = ((b * a.H + h) * a.S + sp) * D;
+      const int64_t row0 = (bw * a.H + h) * a.S + spw;  // staged path: first output row
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out[seg]) + out_off;
+      if (staged) reclaim();
+      if (!prologue) {
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t v[32];
@@ -296,75 +270,346 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_wait_ld();
           uint32_t p[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float2 x = round_bf16_pair(v[2 * i], v[2 * i + 1]);
-            acc = __ffma2_rn(x, x, acc);  // squares of BF16 values are exact in FP32
-            p[i] = pack_bf16(x);
-          }
-          if (want_raw) {
+          for (int i = 0; i < 16; ++i)
+            p[i] = pack_bf16(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])));
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              emit16(raw, valid, 32 * c + 8 * q, make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]));
-          }
-        }
-        if (want_raw && staged) {
-          flush(&om.m[3 + seg], row0);
-          reclaim();
-        }
-        const float r = inv_rms<D>(__fadd_rn(acc.x, acc.y), a.eps);
-        const float2 r2 = splat2(r);
-        const float2 e2 = splat2(seg == 0 ? (float)exp((double)a.scales[h]) : 1.f);
-        const float* wrow = w_s + seg * D;
-        // Pass 2, 16 columns at a time: columns j and j + D/2 of the head are
-        // in this thread; each product and sum rounds like the eager formulation.
-#pragma unroll
-        for (int g = 0; g < HALF / 16; ++g) {
-          uint32_t va[16], vb[16];
-          tmem_ld16(tcol + 16 * g, va);
-          tmem_ld16(tcol + HALF + 16 * g, vb);
-          tmem_wait_ld();
-          uint32_t p1[8], p2[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int j = 16 * g + 2 * i;  // column pair within the first half
-            const float2 x1 = round_bf16_pair(va[2 * i], va[2 * i + 1]);
-            const float2 x2 = round_bf16_pair(vb[2 * i], vb[2 * i + 1]);
-            const float2 wa = ld_pair(wrow, j / 2);
-            const float2 wb = ld_pair(wrow + HALF, j / 2);
-            const float2 c2 = make_float2(cs[j], cs[j + 1]);
-            const float2 s2 = make_float2(sn[j], sn[j + 1]);
-            const float2 y1 = __fmul2_rn(__fmul2_rn(x1, r2), wa);
-            const float2 y2 = __fmul2_rn(__fmul2_rn(x2, r2), wb);
-            float2 o1 = __fadd2_rn(__fmul2_rn(y1, c2), neg2(__fmul2_rn(y2, s2)));
-            float2 o2 = __fadd2_rn(__fmul2_rn(y2, c2), __fmul2_rn(y1, s2));
-            if (seg == 0) {
-              o1 = __fmul2_rn(o1, e2);
-              o2 = __fmul2_rn(o2, e2);
-            }
-            p1[i] = pack_bf16(o1);
-            p2[i] = pack_bf16(o2);
-          }
-          emit16(out, valid, 16 * g, make_uint4(p1[0], p1[1], p1[2], p1[3]));
-          emit16(out, valid, 16 * g + 8, make_uint4(p1[4], p1[5], p1[6], p1[7]));
-          emit16(out, valid, HALF + 16 * g, make_uint4(p2[0], p2[1], p2[2], p2[3]));
-          emit16(out, valid, HALF + 16 * g + 8, make_uint4(p2[4], p2[5], p2[6], p2[7]));
+          for (int q = 0; q < 4; ++q)
+            emit16(out, valid, 32 * c + 8 * q, make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]));
         }
         if (staged) flush(&om.m[seg], row0);
+        continue;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[abuf]);
+      if (GROUPS > SLOTS && hh != head0) {
+#pragma unroll
+        for (int g = 0; g < SLOTS; ++g) load_group(g, g);
+      }
+      // Pass 1: BF16 projection, optional raw store, sum of squares; 32
+      // columns per step, the next step's TMEM loads in flight meanwhile.
+      const bool want_raw = a.raw[seg] != nullptr;
+      __nv_bfloat16* raw = want_raw ? static_cast<__nv_bfloat16*>(a.raw[seg]) + out_off : nullptr;
+      float2 acc = make_float2(0.f, 0.f);
+      uint32_t va[2][16], vb[2][16];
+      tmem_ld16(tcol, va[0]);
+      tmem_ld16(tcol + 16, vb[0]);
+      tmem_wait_ld_regs(va[0], vb[0]);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        const int nb = (c + 1) & 1;
+        if (c + 1 < D / 32) {
+          tmem_ld16(tcol + 32 * (c + 1), va[nb]);
+          tmem_ld16(tcol + 32 * (c + 1) + 16, vb[nb]);
+        }
+        uint32_t p[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          p[i] = pack_bf16(make_float2(__uint_as_float(va[c & 1][2 * i]), __uint_as_float(va[c & 1][2 * i + 1])));
+          p[8 + i] = pack_bf16(make_float2(__uint_as_float(vb[c & 1][2 * i]), __uint_as_float(vb[c & 1][2 * i + 1])));
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x = unpack_bf16(p[i]);
+          acc = __ffma2_rn(x, x, acc);  // squares of BF16 values are exact in FP32
+        }
+        if (want_raw) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            emit16(raw, valid, 32 * c + 8 * q, make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]));
+        }
+        if (c + 1 < D / 32) tmem_wait_ld_regs(va[nb], vb[nb]);
+      }
+      // Pass 2's first group is requested before the raw store's wait.
+      tmem_ld16(tcol, va[0]);
+      tmem_ld16(tcol + HALF, vb[0]);
+      if (want_raw && staged) {
+        flush(&om.m[3 + seg], row0);
+        reclaim();
+      }
+      tmem_wait_ld_regs(va[0], vb[0]);
+      const float r = inv_rms<D>(__fadd_rn(acc.x, acc.y), a.eps);
+      const float2 r2 = splat2(r);
+      const float2 e2 = splat2(seg == 0 ? (float)exp((double)a.scales[h]) : 1.f);
+      const float* wrow = sm.w_s + seg * D;
+      // Pass 2, 16 columns at a time: columns j and j + D/2 of the head are
+      // in this thread; each product and sum rounds like the eager formulation.
+#pragma unroll
+      for (int g = 0; g < GROUPS; ++g) {
+        const int slot = g % SLOTS;
+        const int gb = g & 1, nb = (g + 1) & 1;
+        if (g + 1 < GROUPS) {
+          tmem_ld16(tcol + 16 * (g + 1), va[nb]);
+          tmem_ld16(tcol + HALF + 16 * (g + 1), vb[nb]);
+        }
+        uint32_t p1[8], p2[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int j = 16 * g + 2 * i;  // column pair within the first half
+          const float2 x1 = unpack_bf16(pack_bf16(make_float2(__uint_as_float(va[gb][2 * i]), __uint_as_float(va[gb][2 * i + 1]))));
+          const float2 x2 = unpack_bf16(pack_bf16(make_float2(__uint_as_float(vb[gb][2 * i]), __uint_as_float(vb[gb][2 * i + 1]))));
+          const float2 wa = ld_pair(wrow, j / 2);
+          const float2 wb = ld_pair(wrow + HALF, j / 2);
+          const float2 c2 = make_float2(cs[slot][2 * i], cs[slot][2 * i + 1]);
+          const float2 s2 = make_float2(sn[slot][2 * i], sn[slot][2 * i + 1]);
+          const float2 y1 = __fmul2_rn(__fmul2_rn(x1, r2), wa);
+          const float2 y2 = __fmul2_rn(__fmul2_rn(x2, r2), wb);
+          float2 o1 = __fadd2_rn(__fmul2_rn(y1, c2), neg2(__fmul2_rn(y2, s2)));
+          float2 o2 = __fadd2_rn(__fmul2_rn(y2, c2), __fmul2_rn(y1, s2));
+          if (seg == 0) {
+            o1 = __fmul2_rn(o1, e2);
+            o2 = __fmul2_rn(o2, e2);
+          }
+          p1[i] = pack_bf16(o1);
+          p2[i] = pack_bf16(o2);
+        }
+        if (GROUPS > SLOTS && g + SLOTS < GROUPS) load_group(g + SLOTS, slot);
+        emit16(out, valid, 16 * g, make_uint4(p1[0], p1[1], p1[2], p1[3]));
+        emit16(out, valid, 16 * g + 8, make_uint4(p1[4], p1[5], p1[6], p1[7]));
+        emit16(out, valid, HALF + 16 * g, make_uint4(p2[0], p2[1], p2[2], p2[3]));
+        emit16(out, valid, HALF + 16 * g + 8, make_uint4(p2[4], p2[5], p2[6], p2[7]));
+        if (g + 1 < GROUPS) tmem_wait_ld_regs(va[nb], vb[nb]);
+      }
+      if (staged) flush(&om.m[seg], row0);
     }
-    // Every staged store must have completed before the CTA ends.
-    if (staged && lane == 0) bulk_wait_group0();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if (ROWS == kRowsPair)
+        mbar_arrive_cluster(acc_empty_cluster + abuf * (uint32_t)sizeof(uint64_t));
+      else
+        mbar_arrive(&sm.acc_empty[abuf]);
+    }
+  }
+  // Every staged store must have completed before the CTA ends.
+  if (staged && lane == 0) bulk_wait_group0();
+}
+
+// ---------------------------------------------------------------------------
+// Single-CTA mainloop: one persistent CTA per SM, 128 x 256 tiles.
+template <int D>
+__global__ void __launch_bounds__(RolesSingle::kThreads, 1)
+    qkv_gemm_prologue_kernel(const __grid_constant__ CUtensorMap tm_x,
+                             const __grid_constant__ CUtensorMap tm_w,
+                             const __grid_constant__ OutMaps om,
+                             const __grid_constant__ GemmArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  using R = RolesSingle;
+  const GemmSmem sm =
+      carve_smem<kStagesSingle, kStageBytesSingle, kStagingBufsSingle, R::kEpi>(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesSingle; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], R::kEpi);
+    }
+    fence_mbar_init();
+  }
+  if (warp == R::kMma) {
+    tmem_alloc(sm.tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (a.apply_prologue) {
+    for (int i = threadIdx.x; i < 2 * D; i += R::kThreads) sm.w_s[i] = a.w[i];
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *sm.tmem_slot;
+  const int num_kb = (int)(a.K / BK);
+  bool failed = false;
+
+  if (warp == R::kProducer) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      prefetch_tmap(&tm_x);
+      prefetch_tmap(&tm_w);
+      uint32_t it = 0;
+      for (int64_t tile = blockIdx.x; tile < a.n_tiles && !failed; tile += gridDim.x) {
+        const int32_t m0 = (int32_t)((tile / a.n_tiles_n) * kRowsSingle);
+        const int32_t n0 = (int32_t)((tile % a.n_tiles_n) * BN);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % kStagesSingle;
+          if (!mbar_wait(&sm.empty[s], ((it / kStagesSingle) & 1) ^ 1)) { failed = true; break; }
+          unsigned char* st = sm.ring + s * kStageBytesSingle;
+          mbar_arrive_expect_tx(&sm.full[s], kStageBytesSingle);
+          tma_load_2d(st, &tm_x, kb * BK, m0, &sm.full[s]);
+          tma_load_2d(st + kStageASingle, &tm_w, kb * BK, n0, &sm.full[s]);
+        }
+      }
+    }
+  } else if (warp == R::kMma) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kRowsSingle, BN);
+      uint32_t it = 0, tcount = 0;
+      for (int64_t tile = blockIdx.x; tile < a.n_tiles && !failed; tile += gridDim.x, ++tcount) {
+        const uint32_t abuf = tcount & 1;
+        if (!mbar_wait(&sm.acc_empty[abuf], ((tcount >> 1) & 1) ^ 1)) { failed = true; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + abuf * kAccCols;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % kStagesSingle;
+          if (!mbar_wait(&sm.full[s], (it / kStagesSingle) & 1)) { failed = true; break; }
+          tc_fence_after();
+          const uint32_t st = smem_u32(sm.ring + s * kStageBytesSingle);
+          const uint64_t adesc = smem_desc_k_sw128(st);
+          const uint64_t bdesc = smem_desc_k_sw128(st + kStageASingle);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // +32 bytes along K per step: +2 in the descriptor's start-address field.
+            umma_bf16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          }
+          umma_commit(&sm.empty[s]);  // releases the stage once these MMAs have read it
+        }
+        if (failed) break;
+        umma_commit(&sm.acc_full[abuf]);
+      }
+      // Wait for the last accumulator's MMAs before TMEM may be released.
+      if (tcount > 0 && !failed) {
+        const uint32_t last = tcount - 1;
+        mbar_wait(&sm.acc_full[last & 1], (last >> 1) & 1);
+      }
+    }
+  } else {
+    run_epilogue<D, kRowsSingle, kStagingBufsSingle, R::kEpi, D / 32>(om, a, sm, tmem_base, blockIdx.x, gridDim.x, 0, 0u);
   }
 
   // Teardown: every warp arrives here (also after a timed-out wait).
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == R::kMma) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair mainloop: 2-CTA clusters, 256 x 256 tiles (see the file comment).
+template <int D, int EPI>
+__global__ void __launch_bounds__(Roles<EPI>::kThreads, 1)
+    qkv_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
+                         const __grid_constant__ CUtensorMap tm_w,
+                         const __grid_constant__ OutMaps om,
+                         const __grid_constant__ GemmArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  using C = PairConfig<EPI>;
+  using R = typename C::R;
+  constexpr int kStagesPair = C::kStages;
+  const GemmSmem sm = carve_smem<kStagesPair, kStageBytesPair, kStagingBufsPair, R::kEpi>(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: the CTA that issues the MMAs
+  const int64_t pair = blockIdx.x >> 1;
+  const int64_t n_pairs = gridDim.x >> 1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesPair; ++s) {
+      mbar_init(&sm.full[s], 1);   // even CTA: its producer's arrival + both CTAs' bytes
+      mbar_init(&sm.empty[s], 1);  // one MMA commit per use, in each CTA
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 2 * R::kEpi);  // even CTA: the epilogue warps of both CTAs
+    }
+    fence_mbar_init();
+  }
+  if (warp == R::kMma) {
+    tmem_alloc_pair(sm.tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (a.apply_prologue) {
+    for (int i = threadIdx.x; i < 2 * D; i += R::kThreads) sm.w_s[i] = a.w[i];
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *sm.tmem_slot;
+  const int num_kb = (int)(a.K / BK);
+  constexpr uint32_t kBar = sizeof(uint64_t);
+
+  if (warp == R::kProducer) {
+    // -------------------- TMA producer (both CTAs) --------------------
+    if (lane == 0) {
+      prefetch_tmap(&tm_x);
+      prefetch_tmap(&tm_w);
+      const uint32_t full0 = mapa_shared(smem_u32(sm.full), 0);
+      bool failed = false;
+      uint32_t it = 0;
+      for (int64_t tile = pair; tile < a.n_tiles && !failed; tile += n_pairs) {
+        const int32_t m0 = (int32_t)((tile / a.n_tiles_n) * kRowsPair + rank * 128);
+        const int32_t n0 = (int32_t)((tile % a.n_tiles_n) * BN + rank * (BN / 2));
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % kStagesPair;
+          if (!mbar_wait(&sm.empty[s], ((it / kStagesPair) & 1) ^ 1)) { failed = true; break; }
+          unsigned char* st = sm.ring + s * kStageBytesPair;
+          if (rank == 0) mbar_arrive_expect_tx(&sm.full[s], 2 * kStageBytesPair);
+          tma_load_2d_pair(st, &tm_x, kb * BK, m0, full0 + s * kBar);
+          tma_load_2d_pair(st + kStageAPair, &tm_w, kb * BK, n0, full0 + s * kBar);
+        }
+      }
+      // Drain: wait until the MMA commits of the last uses of every stage have
+      // arrived on this CTA's empty barriers, so none lands after the CTA ends.
+      // (A stage never used passes at once: its wait is for the phase before the first.)
+      for (int j = 0; j < kStagesPair && !failed; ++j, ++it) {
+        const int s = it % kStagesPair;
+        if (!mbar_wait(&sm.empty[s], ((it / kStagesPair) & 1) ^ 1)) failed = true;
+      }
+    }
+  } else if (warp == R::kMma) {
+    // -------------------- MMA issuer (even CTA, one thread) --------------------
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kRowsPair, BN);
+      const uint32_t empty_own = mapa_shared(smem_u32(sm.empty), 0);
+      const uint32_t empty_peer = mapa_shared(smem_u32(sm.empty), 1);
+      const uint32_t accf_own = mapa_shared(smem_u32(sm.acc_full), 0);
+      const uint32_t accf_peer = mapa_shared(smem_u32(sm.acc_full), 1);
+      bool failed = false;
+      uint32_t it = 0, tcount = 0;
+      for (int64_t tile = pair; tile < a.n_tiles && !failed; tile += n_pairs, ++tcount) {
+        const uint32_t abuf = tcount & 1;
+        if (!mbar_wait_cluster(&sm.acc_empty[abuf], ((tcount >> 1) & 1) ^ 1)) { failed = true; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + abuf * kAccCols;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % kStagesPair;
+          if (!mbar_wait(&sm.full[s], (it / kStagesPair) & 1)) { failed = true; break; }
+          tc_fence_after();
+          const uint32_t st = smem_u32(sm.ring + s * kStageBytesPair);
+          const uint64_t adesc = smem_desc_k_sw128(st);
+          const uint64_t bdesc = smem_desc_k_sw128(st + kStageAPair);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          // Release stage s in both CTAs once these MMAs have read it.
+          umma_commit_pair(empty_own + s * kBar);
+          umma_commit_pair(empty_peer + s * kBar);
+        }
+        if (failed) break;
+        umma_commit_pair(accf_own + abuf * kBar);
+        umma_commit_pair(accf_peer + abuf * kBar);
+      }
+      // Wait for the last accumulator's MMAs before TMEM may be released.
+      if (tcount > 0 && !failed) {
+        const uint32_t last = tcount - 1;
+        mbar_wait(&sm.acc_full[last & 1], (last >> 1) & 1);
+      }
+    }
+  } else {
+    run_epilogue<D, kRowsPair, kStagingBufsPair, R::kEpi, C::kSlots>(om, a, sm, tmem_base, pair, n_pairs, (int)rank * 128,
+                               mapa_shared(smem_u32(sm.acc_empty), 0));
+  }
+
+  // Teardown: every thread of both CTAs arrives here (also after a timed-out
+  // wait), so no CTA ends while its peer may still signal its barriers.
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();
+  if (warp == R::kMma) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -405,27 +650,74 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-size_t gemm_smem_bytes(int64_t D) {
-  return 1024 + (size_t)kStages * kStageBytes + (size_t)kEpiWarps * kStagingPerWarp + 256 +
-         (size_t)(2 * D) * 4;
+int sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  return sms;
 }
 
 template <int D>
-cudaError_t launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const OutMaps& om,
-                        const GemmArgs& args, cudaStream_t stream) {
+cudaError_t launch_single(const CUtensorMap& mx, const CUtensorMap& mw, const OutMaps& om,
+                          const GemmArgs& args, cudaStream_t stream) {
   const void* fn = reinterpret_cast<const void*>(&qkv_gemm_prologue_kernel<D>);
-  const size_t smem = gemm_smem_bytes(D);
+  const size_t smem = smem_bytes_for(kStagesSingle, kStageBytesSingle, kStagingBufsSingle,
+                                     RolesSingle::kEpi, D);
   cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  int dev = 0, sms = 0;
-  if ((err = cudaGetDevice(&dev)) != cudaSuccess) return err;
-  if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return err;
+  const int sms = sm_count();
+  if (sms <= 0) return cudaErrorInvalidDevice;
   const int64_t grid = args.n_tiles < sms ? args.n_tiles : sms;
-  qkv_gemm_prologue_kernel<D><<<(unsigned)grid, kGemmThreads, smem, stream>>>(mx, mw, om, args);
+  qkv_gemm_prologue_kernel<D><<<(unsigned)grid, RolesSingle::kThreads, smem, stream>>>(mx, mw, om, args);
   return cudaGetLastError();
 }
 
+// Co-resident 2-CTA clusters of a pair kernel on this device (cached).
+template <int D, int EPI>
+int resident_pairs(const cudaLaunchConfig_t& cfg) {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (dev < 64 && cached[dev] > 0) return cached[dev];
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, qkv_gemm_pair_kernel<D, EPI>, &cfg) != cudaSuccess) return -1;
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+template <int D, int EPI>
+cudaError_t launch_pair(const CUtensorMap& mx, const CUtensorMap& mw, const OutMaps& om,
+                        const GemmArgs& args, cudaStream_t stream) {
+  using C = PairConfig<EPI>;
+  const size_t smem = smem_bytes_for(C::kStages, kStageBytesPair, kStagingBufsPair, EPI, D);
+  cudaError_t err = cudaFuncSetAttribute(qkv_gemm_pair_kernel<D, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return err;
+  const int sms = sm_count();
+  if (sms <= 0) return cudaErrorInvalidDevice;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(sms & ~1));
+  cfg.blockDim = dim3(C::R::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int pairs_max = resident_pairs<D, EPI>(cfg);
+  if (pairs_max <= 0) return cudaErrorInvalidConfiguration;
+  const int64_t pairs = args.n_tiles < pairs_max ? args.n_tiles : pairs_max;
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  return cudaLaunchKernelEx(&cfg, qkv_gemm_pair_kernel<D, EPI>, mx, mw, om, args);
+}
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 0: CTA-pair mainloop (default), 1: single-CTA mainloop.
+int g_gemm_variant = 0;
 
 }  // namespace
 
@@ -442,6 +734,12 @@ cudaError_t read_gemm_device_error(int* value, bool reset) {
 using namespace flash_prologue;
 
 extern "C" {
+
+FLASH_PROLOGUE_API int flash_prologue_set_gemm_variant(int variant) {
+  if (variant != 0 && variant != 1) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  g_gemm_variant = variant;
+  return FLASH_PROLOGUE_OK;
+}
 
 FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(
     const void* x, const void* w, int64_t M, int64_t K, int64_t H, int64_t D, int64_t S,
@@ -467,12 +765,17 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(
         ((sin_strides[0] | sin_strides[1] | cos_strides[0] | cos_strides[1]) & 3) != 0)
       return FLASH_PROLOGUE_ERR_ALIGNMENT;
   }
+  const bool pair = g_gemm_variant == 0;
+  const int rows = pair ? kRowsPair : kRowsSingle;
+  // Per CTA the pair loads 128 rows of X and 128 of W per stage; the single
+  // CTA 128 rows of X and 256 of W.
   CUtensorMap mx, mw;
-  if (!make_map(&mx, x, M, K, BM) || !make_map(&mw, w, 3 * H * D, K, BN)) return FLASH_PROLOGUE_ERR_CUDA;
+  if (!make_map(&mx, x, M, K, 128) || !make_map(&mw, w, 3 * H * D, K, pair ? BN / 2 : BN))
+    return FLASH_PROLOGUE_ERR_CUDA;
   GemmArgs g{};
   g.M = M; g.K = K; g.H = H; g.D = D; g.S = S;
   g.n_tiles_n = 3 * H * D / BN;
-  g.n_tiles = ((M + BM - 1) / BM) * g.n_tiles_n;
+  g.n_tiles = ((M + rows - 1) / rows) * g.n_tiles_n;
   g.w = rmsnorm_weight; g.scales = scales; g.sin = sin; g.cos = cos;
   if (apply_prologue) {
     g.sin_b = sin_strides[0]; g.sin_n = sin_strides[1];
@@ -494,7 +797,15 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(
     for (int i = 0; i < 5; ++i) om.m[i] = mx;  // unused
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t err = (D == 64) ? launch_gemm<64>(mx, mw, om, g, s) : launch_gemm<128>(mx, mw, om, g, s);
+  cudaError_t err;
+  // Pair configurations: 8 epilogue warps for the D = 128 prologue (at D = 64
+  // the 168-register budget of 10 warps would spill), 4 otherwise.
+  if (pair && apply_prologue && D == 128)
+    err = launch_pair<128, 8>(mx, mw, om, g, s);
+  else if (pair)
+    err = (D == 64) ? launch_pair<64, 4>(mx, mw, om, g, s) : launch_pair<128, 4>(mx, mw, om, g, s);
+  else
+    err = (D == 64) ? launch_single<64>(mx, mw, om, g, s) : launch_single<128>(mx, mw, om, g, s);
   return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
 }
 

@@ -205,6 +205,16 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(const void* x, const void* w,
                        float eps, int apply_prologue, void* stream);
 
 /*
+ * Mainloop of flash_prologue_qkv_gemm_fwd (process-wide, not thread-safe; for
+ * tests and tuning). 0 (default): CTA pairs -- 2-CTA clusters running
+ * tcgen05.mma.cta_group::2 on 256 x 256 tiles, each CTA loading half of the
+ * operands; 1: one CTA per SM on 128 x 256 tiles. Both give identical results.
+ * No counterpart in the reference (whose GEMM is a CuTe-DSL sm_120a kernel,
+ * fused_qkv.py:25, 53-594).
+ */
+FLASH_PROLOGUE_API int flash_prologue_set_gemm_variant(int variant);
+
+/*
  * Backward prologue that allocates nothing: the same computation and results
  * as flash_prologue_bwd, without the `workspace` arguments. For callers that
  * cannot allocate device memory per call (runtimes that plan all device memory

@@ -144,3 +144,22 @@ def test_config5_full_size_sampled_rows():
                              term_magnitudes(*args)):
         ok, stats = check_outputs(got.cpu(), exp, mag)
         assert ok and stats["exact_frac"] > 0.99, stats
+
+
+@pytest.mark.parametrize("B,N,hidden,H,D", [(1, 200, 128, 8, 64), (3, 128, 256, 2, 128),
+                                            (1, 1000, 512, 4, 128), (2, 96, 192, 4, 64)])
+def test_cta_pair_and_single_cta_mainloops_agree(B, N, hidden, H, D):
+    """The 2-CTA (cta_group::2, 256-row tiles) and single-CTA mainloops give identical outputs."""
+    from flash_attn_prologue_b200 import _lib
+    x, w, rw, sc, sin, cos = _problem(B, N, hidden, H, D, seed=31 + N)
+    outs = []
+    try:
+        for variant in (1, 0):
+            _lib.set_gemm_variant(variant)
+            outs.append(fap.fused_qkv_epilogue(x, w, rw, sc, sin, cos))
+            torch.cuda.synchronize()
+            assert _lib.device_error(reset=True) == 0
+    finally:
+        _lib.set_gemm_variant(0)
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
