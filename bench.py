@@ -398,7 +398,31 @@ def run_extras(device, steps=20):
         _event_ms(lambda: inv_fwd(q4, k4, w, s, s4, c4, 1e-5), steps))
     hbm("c2_inverse_bwd", T * (H * D * 2 * 6 + D * 4 + 2 * H * 4),
         _event_ms(lambda: inv_bwd(qo, ko, w, s, s4, c4, g4q, g4k, rq, rk, 1e-5), steps))
-    del buf, q4, k4, g4q, g4k, qo, ko, rq, rk
+    del q4, k4, qo, ko, rq, rk
+    # C2 training step with the QKV gradient: forward + autograd backward to the
+    # [T, 3, H, D] buffer, V's gradient included. Through slice views
+    # (q, k, v = qkv.unbind(1) + qknorm_rope_scale: autograd gathers dq, dk, dv
+    # into the buffer's gradient) and through qknorm_rope_scale_qkv (the kernel
+    # writes dq, dk into the gradient buffer's slots; dv is copied into its slot).
+    gq3, gk3 = (t[0].permute(1, 0, 2) for t in (g4q, g4k))
+    gv3 = torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16)
+    s2, c2 = sin, cos
+
+    def step_slices():
+        x = buf.detach().requires_grad_()
+        q, k, v = x.unbind(1)
+        qo_, ko_ = qknorm_rope_scale(q, k, w, s, s2, c2, backend="cute")
+        return torch.autograd.grad((qo_, ko_, v), x, (gq3, gk3, gv3))
+
+    def step_packed():
+        x = buf.detach().requires_grad_()
+        qo_, ko_, v = fap.qknorm_rope_scale_qkv(x, w, s, s2, c2)
+        return torch.autograd.grad((qo_, ko_, v), x, (gq3, gk3, gv3))
+
+    step_bytes = T * (FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN + H * D * 2 * 2)  # + dv read/write
+    for name, fn in (("c2_qkv_step_slice_views", step_slices), ("c2_qkv_step_packed_gradient", step_packed)):
+        hbm(name, step_bytes, _event_ms(fn, steps))
+    del buf, g4q, g4k, gq3, gk3, gv3
     # C5
     T, hidden, H, D = 65536, 2048, 16, 128
     x = torch.randn(1, T, hidden, generator=g, device=device).to(torch.bfloat16)
@@ -501,6 +525,24 @@ def run_e2e(args, T, device, w, s, world):
             "path": "qknorm_rope_scale(backend='cute') -> torch.library op -> C ABI"}
 
 
+def run_c5_profile_case(T):
+    """Three launches of the fused QKV GEMM + prologue at C5's hidden size and heads."""
+    import flash_attn_prologue_b200 as fap
+    from flash_attn_prologue_b200 import _lib
+    hidden, H, D = 2048, 16, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(1, T, hidden, generator=g, device="cuda").to(torch.bfloat16)
+    wq = (0.02 * torch.randn(3 * H * D, hidden, generator=g, device="cuda")).to(torch.bfloat16)
+    sin, cos = rope_tables(torch.arange(T, device="cuda"), D, 10000.0)
+    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device="cuda")
+    s = 0.1 * torch.randn(H, 1, 1, generator=g, device="cuda")
+    for _ in range(3):
+        fap.fused_qkv_epilogue(x, wq, w, s, sin, cos)
+    torch.cuda.synchronize()
+    if _lib.device_error(reset=True) != 0:
+        raise SystemExit("device error word set")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -514,9 +556,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the C1/C3/C4/C5 timings reported beside the headline")
+    ap.add_argument("--c5-profile-tokens", type=int, default=0,
+                    help="only run the fused QKV GEMM + prologue (C5 shapes, this many tokens) three "
+                         "times and exit: the small case an ncu capture of that kernel uses")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.c5_profile_tokens:
+        run_c5_profile_case(args.c5_profile_tokens)
+        return
     if args.impl == "reference":
         # The reference path is CPU code: rank 0 runs it, other ranks exit at once.
         world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -8,7 +8,7 @@ environment variable.
 """
 from importlib import import_module
 
-from .functional import prepare_backend, qknorm_rope_scale
+from .functional import prepare_backend, qknorm_rope_scale, qknorm_rope_scale_qkv
 from .layers.RMSNorm import RMSNormRoPEScale
 
 __version__ = "0.2.0"
@@ -22,7 +22,7 @@ _LAZY = {
     "fused_qkv": ("fused_qkv", "fused_qkv_op"),
     "fused_qkv_epilogue": ("fused_qkv", "fused_qkv_epilogue_op"),
 }
-__all__ = ["qknorm_rope_scale", "prepare_backend", "RMSNormRoPEScale", *_LAZY]
+__all__ = ["qknorm_rope_scale", "qknorm_rope_scale_qkv", "prepare_backend", "RMSNormRoPEScale", *_LAZY]
 
 
 def __getattr__(name):

@@ -24,18 +24,11 @@ def prepare_backend(backend: str = "native") -> None:
         from . import fused_epilogue  # noqa: F401
 
 
-def qknorm_rope_scale(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5, *, backend="native"):
-    """Normalize Q/K, apply half-width RoPE, and multiply Q by exp(scales).
+def _validate(q, k, rmsnorm_weight, scales, sin, cos, eps, backend):
+    """The reference frontend's checks, in its order (functional.py:29-70).
 
-    Q/K: matching packed [T,H,D] or dense [B,H,N,D], BF16/FP16/FP32.
-    Weight: [2,1,D]. Log-scales: [H,1,1]. Both must be FP32.
-    Packed sin/cos: [T,D/2] or [T,1,D/2]. Dense: [N,D/2], [B,N,D/2], or
-    [B,1,N,D/2]; singleton B/N broadcasting is supported. Frequencies are FP32;
-    positions and RoPE resets are the caller's (per-row op: no cu_seqlens).
-    All arithmetic through the final cast is FP32. Inputs are never mutated.
-    ``cute``: CUDA, BF16/FP16/FP32, D in (32, 64, 128, 256), up to 512 heads,
-    any eps > 0; no sin/cos gradients. Strided q/k views (e.g. slices of a
-    fused QKV buffer) are read in place.
+    Returns sin/cos reshaped for broadcasting against q/k and the scale view
+    of the native formulation; raises the reference's ValueError texts.
     """
     if backend not in ("native", "cute"):
         raise ValueError("backend must be 'native' or 'cute'")
@@ -79,7 +72,26 @@ def qknorm_rope_scale(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5, *, backe
             raise ValueError("CuTe supports at most 512 heads")
         if sin.requires_grad or cos.requires_grad:
             raise ValueError("CuTe does not implement frequency gradients; use native")
+    return sin, cos, scale
+
+
+def qknorm_rope_scale(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5, *, backend="native"):
+    """Normalize Q/K, apply half-width RoPE, and multiply Q by exp(scales).
+
+    Q/K: matching packed [T,H,D] or dense [B,H,N,D], BF16/FP16/FP32.
+    Weight: [2,1,D]. Log-scales: [H,1,1]. Both must be FP32.
+    Packed sin/cos: [T,D/2] or [T,1,D/2]. Dense: [N,D/2], [B,N,D/2], or
+    [B,1,N,D/2]; singleton B/N broadcasting is supported. Frequencies are FP32;
+    positions and RoPE resets are the caller's (per-row op: no cu_seqlens).
+    All arithmetic through the final cast is FP32. Inputs are never mutated.
+    ``cute``: CUDA, BF16/FP16/FP32, D in (32, 64, 128, 256), up to 512 heads,
+    any eps > 0; no sin/cos gradients. Strided q/k views (e.g. slices of a
+    fused QKV buffer) are read in place.
+    """
+    sin, cos, scale = _validate(q, k, rmsnorm_weight, scales, sin, cos, eps, backend)
+    if backend == "cute":
         prepare_backend("cute")
+        d = q.shape[-1]
         if q.ndim == 3:
             q4, k4 = q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None]
             s4, c4 = sin.permute(1, 0, 2)[None], cos.permute(1, 0, 2)[None]
@@ -107,3 +119,74 @@ def qknorm_rope_scale(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5, *, backe
 
     return ((transform(q, rmsnorm_weight[0]) * scale.exp()).to(q.dtype),
             transform(k, rmsnorm_weight[1]).to(k.dtype))
+
+
+def _cute_tables(sin, cos, packed, B, N, half):
+    """sin/cos (as reshaped by _validate) as [B|1, 1, N, D/2] views for the op."""
+    if packed:
+        sin, cos = sin.permute(1, 0, 2)[None], cos.permute(1, 0, 2)[None]
+    sin = sin.expand(sin.shape[0], 1, N, half)
+    return sin, cos.expand_as(sin)
+
+
+class _QKVPrologue(torch.autograd.Function):
+    """Prologue on the Q/K slots of a packed QKV tensor, V passed through.
+
+    The backward writes dq, dk and dv straight into one gradient tensor laid
+    out like qkv, instead of autograd gathering three separate gradients of
+    slice views into it (which re-reads and re-writes dq and dk).
+    """
+
+    @staticmethod
+    def forward(ctx, qkv5, rmsnorm_weight, scales, sin4, cos4, eps):
+        q4 = qkv5[:, :, 0].permute(0, 2, 1, 3)
+        k4 = qkv5[:, :, 1].permute(0, 2, 1, 3)
+        out_q, out_k = torch.ops.flash_prologue.qknorm_rope_scale_cute(
+            q4, k4, rmsnorm_weight, scales, sin4, cos4, eps)
+        ctx.save_for_backward(qkv5, rmsnorm_weight, scales, sin4, cos4)
+        ctx.eps = eps
+        return out_q, out_k, qkv5[:, :, 2].permute(0, 2, 1, 3)
+
+    @staticmethod
+    def backward(ctx, grad_q, grad_k, grad_v):
+        qkv5, rmsnorm_weight, scales, sin4, cos4 = ctx.saved_tensors
+        gv = None if grad_v is None else grad_v.permute(0, 2, 1, 3)
+        grad_qkv, dw, ds = torch.ops.flash_prologue.qknorm_rope_scale_qkv_backward(
+            qkv5, rmsnorm_weight, scales, sin4, cos4, grad_q, grad_k, gv, ctx.eps)
+        return grad_qkv, dw, ds, None, None, None
+
+
+def qknorm_rope_scale_qkv(qkv, rmsnorm_weight, scales, sin, cos, eps=1e-5, *, backend="cute"):
+    """qknorm_rope_scale on the Q and K slots of a fused QKV activation; returns (q, k, v).
+
+    qkv: packed [T, 3, H, D] or batched [B, N, 3, H, D] (a QKV projection's
+    output viewed as heads; slot 0 = Q, 1 = K, 2 = V). Returns q_out, k_out and
+    v in the layouts of qknorm_rope_scale: packed [T, H, D], batched
+    [B, H, N, D] (v is a view of qkv). Other arguments and checks as
+    qknorm_rope_scale. With ``cute`` the backward produces the gradient of qkv
+    as one tensor: the kernel writes dq and dk into its Q and K slots and the
+    gradient of v lands in its V slot (zeros when v is unused), so no
+    per-slice gradients are gathered afterwards. ``native`` is the reference
+    formulation on the unbound slices.
+    """
+    if qkv.ndim not in (4, 5) or qkv.shape[-3] != 3:
+        raise ValueError("qkv must be packed [T,3,H,D] or batched [B,N,3,H,D]")
+    packed = qkv.ndim == 4
+    q, k, v = qkv.unbind(-3)
+    if not packed:
+        q, k, v = (t.transpose(1, 2) for t in (q, k, v))
+    sin, cos, _ = _validate(q, k, rmsnorm_weight, scales, sin, cos, eps, backend)
+    if backend == "native":
+        q_out, k_out = qknorm_rope_scale(q, k, rmsnorm_weight, scales, sin, cos, eps, backend="native")
+        return q_out, k_out, v
+    prepare_backend("cute")
+    qkv5 = qkv[None] if packed else qkv
+    if qkv5.stride(-1) != 1:
+        qkv5 = qkv5.contiguous()
+    B, N, _, H, D = qkv5.shape
+    sin4, cos4 = _cute_tables(sin, cos, packed, B, N, D // 2)
+    out_q, out_k, v4 = _QKVPrologue.apply(qkv5, rmsnorm_weight, scales, sin4, cos4, eps)
+    if packed:
+        return (out_q.squeeze(0).permute(1, 0, 2), out_k.squeeze(0).permute(1, 0, 2),
+                v4.squeeze(0).permute(1, 0, 2))
+    return out_q, out_k, v4

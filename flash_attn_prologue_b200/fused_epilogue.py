@@ -8,7 +8,11 @@ Registers, under the reference's names and schemas:
   fused_epilogue.py:1304-1423, fake :1425-1437);
 * the autograd link between them (reference: fused_epilogue.py:1440-1458);
 * ``flash_prologue::qknorm_rope_scale_cute_inverse`` / ``_inverse_backward``
-  and their autograd link (reference: fused_epilogue.py:2560-2805).
+  and their autograd link (reference: fused_epilogue.py:2560-2805);
+* ``flash_prologue::qknorm_rope_scale_qkv_backward``: the backward of the
+  prologue on a fused [B, N, 3, H, D] QKV activation, producing its gradient
+  as one tensor (no reference counterpart; the reference returns compact
+  dq/dk, fused_epilogue.py:1399-1402, which autograd then gathers).
 
 Raw-op contract kept from the reference: q/k are 4-D ``[B, H, N, D]`` views
 with channel stride 1 and no expanded (stride-0) dimension, rejected with the
@@ -21,7 +25,7 @@ backward), any ``eps > 0`` and D in {32, 64, 128, 256} with BF16/FP16/FP32 are
 accepted, and the weight/scale gradients are reduced in a fixed order (no float
 atomics). Nothing here runs on the CPU: the device work is the CUDA library.
 """
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 
@@ -426,3 +430,76 @@ def _inverse_backward(ctx, grad_q, grad_k, grad_rms_q, grad_rms_k):
 
 torch.library.register_autograd("flash_prologue::qknorm_rope_scale_cute_inverse", _inverse_backward,
                                 setup_context=_inverse_setup_context)
+
+
+# ---------------------------------------------------------------------------
+# Backward for a fused QKV activation: one gradient tensor laid out like qkv.
+
+@torch.library.custom_op("flash_prologue::qknorm_rope_scale_qkv_backward", mutates_args=())
+def qknorm_rope_scale_qkv_backward_op(
+    qkv: torch.Tensor,
+    rmsnorm_weight: torch.Tensor,
+    scales: torch.Tensor,
+    sin: torch.Tensor,
+    cos: torch.Tensor,
+    grad_q_out: Optional[torch.Tensor],
+    grad_k_out: Optional[torch.Tensor],
+    grad_v: Optional[torch.Tensor],
+    eps: float = 1e-5,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(grad_qkv, dw, ds) for qkv [B, N, 3, H, D].
+
+    grad_q_out / grad_k_out are the gradients of the prologue outputs as
+    [B, H, N, D] views and grad_v that of the V slot as [B, N, H, D] (None =
+    zero). grad_qkv has qkv's memory order; the backward kernel writes dq and
+    dk into its Q and K slots through strided output views and grad_v is
+    copied into its V slot, so the caller needs no gather of slice gradients.
+    """
+    if qkv.ndim != 5 or qkv.shape[2] != 3:
+        raise ValueError("qkv must be [B,N,3,H,D]")
+    grad_qkv = torch.empty_strided(qkv.shape, _get_compact_strides(qkv.shape, qkv.stride()),
+                                   dtype=qkv.dtype, device=qkv.device)
+    q4 = qkv[:, :, 0].permute(0, 2, 1, 3)
+    k4 = qkv[:, :, 1].permute(0, 2, 1, 3)
+    _check_raw(q4, k4)
+    _check_common(q4, k4, rmsnorm_weight, scales, sin, cos, eps)
+    B, H, N, D = (int(x) for x in q4.shape)
+    dq4 = grad_qkv[:, :, 0].permute(0, 2, 1, 3)
+    dk4 = grad_qkv[:, :, 1].permute(0, 2, 1, 3)
+    grad_w = torch.empty((2, 1, D), dtype=torch.float32, device=qkv.device)
+    grad_s = torch.empty((H, 1, 1), dtype=torch.float32, device=qkv.device)
+    gq = _grad_view(grad_q_out, q4)
+    gk = _grad_view(grad_k_out, k4)
+    sin4, sin_str = _table(sin, B, N, D // 2)
+    cos4, cos_str = _table(cos, B, N, D // 2)
+    w = rmsnorm_weight.float().contiguous()
+    s = scales.float().contiguous()
+    lib = _lib.load()
+    with _DeviceGuard(qkv.device):
+        nbytes = bwd_workspace_bytes(B, H, N, D, qkv.dtype) if q4.numel() else 0
+        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=qkv.device)
+        status = lib.flash_prologue_bwd(
+            _lib.ptr(q4), _lib.strides4(q4), _lib.ptr(k4), _lib.strides4(k4),
+            _lib.ptr(w), _lib.ptr(s),
+            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+            _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
+            _lib.ptr(dq4), _lib.strides4(dq4), _lib.ptr(dk4), _lib.strides4(dk4),
+            _lib.ptr(grad_w), _lib.ptr(grad_s),
+            _lib.ptr(workspace), workspace.numel(),
+            B, H, N, D, float(eps), _lib.DTYPE_CODES[qkv.dtype], _lib.stream_of(qkv.device))
+    _lib.check(status, "flash_prologue_bwd")
+    if grad_v is None:
+        grad_qkv[:, :, 2].zero_()
+    else:
+        grad_qkv[:, :, 2].copy_(grad_v)
+    return grad_qkv, grad_w, grad_s
+
+
+@qknorm_rope_scale_qkv_backward_op.register_fake
+def _qknorm_rope_scale_qkv_backward_fake(qkv, rmsnorm_weight, scales, sin, cos, grad_q_out,
+                                         grad_k_out, grad_v, eps=1e-5):
+    D, H = qkv.shape[-1], qkv.shape[-2]
+    return (torch.empty_strided(qkv.shape, _get_compact_strides(qkv.shape, qkv.stride()),
+                                dtype=qkv.dtype, device=qkv.device),
+            torch.empty((2, 1, D), dtype=torch.float32, device=qkv.device),
+            torch.empty((H, 1, 1), dtype=torch.float32, device=qkv.device))

@@ -1,0 +1,89 @@
+"""qknorm_rope_scale_qkv: the prologue on the Q/K slots of a fused QKV activation.
+
+CPU: the ``native`` path equals the reference frontend on the unbound slices
+(flash_attn_prologue/functional.py:14-94). GPU: the ``cute`` path's outputs
+are bit-identical to qknorm_rope_scale on the slice views, and its single
+gradient tensor equals, bit for bit, the gradient autograd gathers from the
+slice views (dq, dk from the same kernel; dv in the V slot; zeros when v is
+unused); the parameter gradients are identical too.
+"""
+import math
+
+import pytest
+import torch
+
+import flash_attn_prologue_b200 as fap
+
+
+def _problem(shape, dtype=torch.bfloat16, seed=0, device="cpu"):
+    g = torch.Generator().manual_seed(seed)
+    H, D = shape[-2], shape[-1]
+    qkv = torch.randn(shape, generator=g).to(dtype)
+    w = 1 + 0.2 * torch.randn(2, 1, D, generator=g)
+    s = 0.2 * torch.randn(H, 1, 1, generator=g) - math.log(D) / 2
+    n = shape[0] if len(shape) == 4 else shape[1]
+    ang = torch.rand(n, D // 2, generator=g) * 6.0
+    return [t.to(device) for t in (qkv, w, s, ang.sin(), ang.cos())]
+
+
+def _slices(qkv):
+    q, k, v = qkv.unbind(-3)
+    if qkv.ndim == 5:
+        q, k, v = (t.transpose(1, 2) for t in (q, k, v))
+    return q, k, v
+
+
+@pytest.mark.parametrize("shape", [(37, 3, 4, 32), (2, 19, 3, 2, 64)])
+def test_native_path_matches_frontend_on_slices(shape):
+    qkv, w, s, sin, cos = _problem(shape)
+    q_out, k_out, v = fap.qknorm_rope_scale_qkv(qkv, w, s, sin, cos, backend="native")
+    q, k, v_ref = _slices(qkv)
+    rq, rk = fap.qknorm_rope_scale(q, k, w, s, sin, cos, backend="native")
+    assert torch.equal(q_out, rq) and torch.equal(k_out, rk) and torch.equal(v, v_ref)
+
+
+def test_rejects_bad_qkv_shapes():
+    qkv, w, s, sin, cos = _problem((8, 3, 2, 32))
+    with pytest.raises(ValueError):
+        fap.qknorm_rope_scale_qkv(qkv[:, :2], w, s, sin, cos, backend="native")
+    with pytest.raises(ValueError):
+        fap.qknorm_rope_scale_qkv(qkv[0], w, s, sin, cos, backend="native")
+    with pytest.raises(ValueError, match="FP32"):
+        fap.qknorm_rope_scale_qkv(qkv, w.double(), s, sin, cos, backend="native")
+
+
+def _grads_via_slices(qkv, w, s, sin, cos, gq, gk, gv):
+    x = qkv.detach().clone().requires_grad_()
+    wl, sl = w.detach().clone().requires_grad_(), s.detach().clone().requires_grad_()
+    q, k, v = _slices(x)
+    q_out, k_out = fap.qknorm_rope_scale(q, k, wl, sl, sin, cos, backend="cute")
+    outs, grads = (q_out, k_out), (gq, gk)
+    if gv is not None:
+        outs, grads = outs + (v,), grads + (gv,)
+    return (q_out, k_out, v), torch.autograd.grad(outs, (x, wl, sl), grads)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(1000, 3, 16, 64), (3, 77, 3, 4, 128), (513, 3, 8, 32)])
+@pytest.mark.parametrize("use_v", [True, False])
+def test_cute_gradient_equals_gathered_slice_gradients(shape, use_v):
+    qkv, w, s, sin, cos = _problem(shape, seed=len(shape) + shape[-1], device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    gq, gk, gv = (torch.randn(_slices(qkv)[0].shape, generator=g, device="cuda").to(qkv.dtype)
+                  for _ in range(3))
+    gv = gv if use_v else None
+    ref_outs, ref_grads = _grads_via_slices(qkv, w, s, sin, cos, gq, gk, gv)
+    x = qkv.detach().clone().requires_grad_()
+    wl, sl = w.detach().clone().requires_grad_(), s.detach().clone().requires_grad_()
+    q_out, k_out, v = fap.qknorm_rope_scale_qkv(x, wl, sl, sin, cos)
+    assert torch.equal(q_out, ref_outs[0]) and torch.equal(k_out, ref_outs[1])
+    assert torch.equal(v, ref_outs[2]) and v.data_ptr() == x[..., 2, :, :].data_ptr()
+    outs, grads = (q_out, k_out), (gq, gk)
+    if gv is not None:
+        outs, grads = outs + (v,), grads + (gv,)
+    got = torch.autograd.grad(outs, (x, wl, sl), grads)
+    torch.cuda.synchronize()
+    for a, b in zip(got, ref_grads):
+        assert a.shape == b.shape and torch.equal(a, b)
+    if gv is None:
+        assert float(got[0][..., 2, :, :].abs().max()) == 0.0
