@@ -21,6 +21,10 @@ _LAZY = {
                                                    "qknorm_rope_scale_cute_inverse_backward_op"),
     "fused_qkv": ("fused_qkv", "fused_qkv_op"),
     "fused_qkv_epilogue": ("fused_qkv", "fused_qkv_epilogue_op"),
+    "fused_qkv_epilogue_ckp": ("fused_qkv", "fused_qkv_epilogue_ckp_op"),
+    "matmul_bwd_dx": ("fused_qkv", "matmul_bwd_dx"),
+    "matmul_bwd_dw": ("fused_qkv", "matmul_bwd_dw"),
+    "fused_qkv_backward": ("fused_qkv", "fused_qkv_backward"),
 }
 __all__ = ["qknorm_rope_scale", "qknorm_rope_scale_qkv", "prepare_backend", "RMSNormRoPEScale", *_LAZY]
 

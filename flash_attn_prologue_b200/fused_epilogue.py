@@ -435,6 +435,41 @@ torch.library.register_autograd("flash_prologue::qknorm_rope_scale_cute_inverse"
 # ---------------------------------------------------------------------------
 # Backward for a fused QKV activation: one gradient tensor laid out like qkv.
 
+def backward_into(q4, k4, rmsnorm_weight, scales, sin, cos, grad_q_out, grad_k_out, dq4, dk4,
+                  eps=1e-5):
+    """The prologue backward writing dq / dk into the given [B, H, N, D] views.
+
+    dq4 / dk4 may be strided views of a larger buffer (the slots of a packed
+    gradient); returns (d rmsnorm_weight [2, 1, D], d scales [H, 1, 1]).
+    """
+    _check_raw(q4, k4)
+    _check_common(q4, k4, rmsnorm_weight, scales, sin, cos, eps)
+    B, H, N, D = (int(x) for x in q4.shape)
+    grad_w = torch.empty((2, 1, D), dtype=torch.float32, device=q4.device)
+    grad_s = torch.empty((H, 1, 1), dtype=torch.float32, device=q4.device)
+    gq = _grad_view(grad_q_out, q4)
+    gk = _grad_view(grad_k_out, k4)
+    sin4, sin_str = _table(sin, B, N, D // 2)
+    cos4, cos_str = _table(cos, B, N, D // 2)
+    w = rmsnorm_weight.float().contiguous()
+    s = scales.float().contiguous()
+    lib = _lib.load()
+    with _DeviceGuard(q4.device):
+        nbytes = bwd_workspace_bytes(B, H, N, D, q4.dtype) if q4.numel() else 0
+        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q4.device)
+        status = lib.flash_prologue_bwd(
+            _lib.ptr(q4), _lib.strides4(q4), _lib.ptr(k4), _lib.strides4(k4),
+            _lib.ptr(w), _lib.ptr(s),
+            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+            _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
+            _lib.ptr(dq4), _lib.strides4(dq4), _lib.ptr(dk4), _lib.strides4(dk4),
+            _lib.ptr(grad_w), _lib.ptr(grad_s),
+            _lib.ptr(workspace), workspace.numel(),
+            B, H, N, D, float(eps), _lib.DTYPE_CODES[q4.dtype], _lib.stream_of(q4.device))
+    _lib.check(status, "flash_prologue_bwd")
+    return grad_w, grad_s
+
+
 @torch.library.custom_op("flash_prologue::qknorm_rope_scale_qkv_backward", mutates_args=())
 def qknorm_rope_scale_qkv_backward_op(
     qkv: torch.Tensor,
@@ -461,33 +496,10 @@ def qknorm_rope_scale_qkv_backward_op(
                                    dtype=qkv.dtype, device=qkv.device)
     q4 = qkv[:, :, 0].permute(0, 2, 1, 3)
     k4 = qkv[:, :, 1].permute(0, 2, 1, 3)
-    _check_raw(q4, k4)
-    _check_common(q4, k4, rmsnorm_weight, scales, sin, cos, eps)
-    B, H, N, D = (int(x) for x in q4.shape)
     dq4 = grad_qkv[:, :, 0].permute(0, 2, 1, 3)
     dk4 = grad_qkv[:, :, 1].permute(0, 2, 1, 3)
-    grad_w = torch.empty((2, 1, D), dtype=torch.float32, device=qkv.device)
-    grad_s = torch.empty((H, 1, 1), dtype=torch.float32, device=qkv.device)
-    gq = _grad_view(grad_q_out, q4)
-    gk = _grad_view(grad_k_out, k4)
-    sin4, sin_str = _table(sin, B, N, D // 2)
-    cos4, cos_str = _table(cos, B, N, D // 2)
-    w = rmsnorm_weight.float().contiguous()
-    s = scales.float().contiguous()
-    lib = _lib.load()
-    with _DeviceGuard(qkv.device):
-        nbytes = bwd_workspace_bytes(B, H, N, D, qkv.dtype) if q4.numel() else 0
-        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=qkv.device)
-        status = lib.flash_prologue_bwd(
-            _lib.ptr(q4), _lib.strides4(q4), _lib.ptr(k4), _lib.strides4(k4),
-            _lib.ptr(w), _lib.ptr(s),
-            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
-            _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
-            _lib.ptr(dq4), _lib.strides4(dq4), _lib.ptr(dk4), _lib.strides4(dk4),
-            _lib.ptr(grad_w), _lib.ptr(grad_s),
-            _lib.ptr(workspace), workspace.numel(),
-            B, H, N, D, float(eps), _lib.DTYPE_CODES[qkv.dtype], _lib.stream_of(qkv.device))
-    _lib.check(status, "flash_prologue_bwd")
+    grad_w, grad_s = backward_into(q4, k4, rmsnorm_weight, scales, sin, cos, grad_q_out, grad_k_out,
+                                   dq4, dk4, eps)
     if grad_v is None:
         grad_qkv[:, :, 2].zero_()
     else:
