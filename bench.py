@@ -353,8 +353,14 @@ def run_extras(device, steps=20):
     sin, cos = rope_tables(torch.arange(T, device=device), D, 10000.0)
     w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
     s = torch.zeros(H, 1, 1, device=device)
-    hbm("c1_fwd", T * (H * D * 2 * 4 + D * 4),
-        _event_ms(lambda: qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute"), steps))
+    c1_bytes = T * (H * D * 2 * 4 + D * 4)
+    hbm("c1_fwd", c1_bytes, _event_ms(lambda: qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute"), steps))
+    # The same call captured once into a CUDA graph and replayed: the kernel
+    # without the Python / dispatch overhead of each eager call.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute")
+    hbm("c1_fwd_graph_replay", c1_bytes, _event_ms(graph.replay, max(steps, 200)))
     # C3
     B, H, S, D = 8, 32, 8192, 128
     q, k = (torch.randn(B, H, S, D, generator=g, device=device).to(torch.bfloat16) for _ in range(2))
