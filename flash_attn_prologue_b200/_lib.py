@@ -55,6 +55,7 @@ SIGNATURES = {
                                      ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
     "flash_prologue_set_path": ([ctypes.c_int], ctypes.c_int),
     "flash_prologue_set_gemm_variant": ([ctypes.c_int], ctypes.c_int),
+    "flash_prologue_selftest_wait_timeout": ([ctypes.c_uint32, _vp], ctypes.c_int),
     "flash_prologue_device_error": ([ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
     "flash_prologue_bwd": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,
                             _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
@@ -99,6 +100,12 @@ def set_path(mode: int) -> None:
 def set_gemm_variant(variant: int) -> None:
     """Fused QKV GEMM mainloop: 0 = CTA pairs (default), 1 = one CTA per SM."""
     check(load().flash_prologue_set_gemm_variant(int(variant)), "flash_prologue_set_gemm_variant")
+
+
+def selftest_wait_timeout(tries: int = 4096) -> None:
+    """Runs a bounded wait that times out on purpose (sets the device error word)."""
+    check(load().flash_prologue_selftest_wait_timeout(int(tries), stream_of(torch.device("cuda"))),
+          "flash_prologue_selftest_wait_timeout")
 
 
 def device_error(reset: bool = True) -> int:

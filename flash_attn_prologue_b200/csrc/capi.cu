@@ -235,6 +235,13 @@ FLASH_PROLOGUE_API int flash_prologue_device_error(int* value, int reset) {
   return FLASH_PROLOGUE_OK;
 }
 
+FLASH_PROLOGUE_API int flash_prologue_selftest_wait_timeout(uint32_t tries, void* stream) {
+  if (tries == 0 || tries > (1u << 22)) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  return launch_selftest_wait_timeout(tries, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? FLASH_PROLOGUE_OK
+             : FLASH_PROLOGUE_ERR_CUDA;
+}
+
 FLASH_PROLOGUE_API int flash_prologue_set_path(int mode) {
   if (mode != 0 && mode != 1) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   g_path_mode = mode;

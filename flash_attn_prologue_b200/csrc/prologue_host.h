@@ -108,6 +108,8 @@ size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv = 
 // prologue kernels and of the fused QKV GEMM.
 cudaError_t read_device_error(int* value, bool reset);
 cudaError_t read_gemm_device_error(int* value, bool reset);
+// One thread waits (bounded by `tries` polls) on a barrier nothing arrives at.
+cudaError_t launch_selftest_wait_timeout(uint32_t tries, cudaStream_t stream);
 int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype, bool inv = false);
 cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream);
 cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype, int D,

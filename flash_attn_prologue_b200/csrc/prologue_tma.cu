@@ -451,6 +451,34 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
 }
 
 // ---------------------------------------------------------------------------
+// Self-test of the bounded-wait path: one thread waits on an mbarrier that
+// nothing arrives at. After `tries` polls it gives up, records the timeout in
+// this translation unit's error word (the word the pipelined kernels use) and
+// returns, exactly as a protocol failure would; nothing faults or hangs.
+__global__ void __launch_bounds__(32) selftest_wait_timeout_kernel(uint32_t tries) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  const uint32_t a = smem_u32(&bar);
+  for (uint32_t i = 0; i < tries; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done) : "r"(a), "r"(0u), "r"(kSuspendHintNs) : "memory");
+    if (done) return;
+  }
+  atomicExch(&g_device_error, kDeviceErrorTimeout);
+}
+
+cudaError_t launch_selftest_wait_timeout(uint32_t tries, cudaStream_t stream) {
+  selftest_wait_timeout_kernel<<<1, 32, 0, stream>>>(tries);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 
 cudaError_t read_device_error(int* value, bool reset) {

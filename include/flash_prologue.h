@@ -261,6 +261,16 @@ FLASH_PROLOGUE_API int flash_prologue_set_path(int mode);
  */
 FLASH_PROLOGUE_API int flash_prologue_device_error(int* value, int reset);
 
+/*
+ * Self-test of failure detection: launches one thread that waits, bounded, on
+ * an mbarrier that nothing arrives at. After `tries` polls (1 .. 2^22, each
+ * suspended up to ~1 us) it gives up and records the timeout in the device
+ * error word exactly as a stalled pipelined kernel would, then returns: the
+ * context stays usable and flash_prologue_device_error() reports 1. Nothing
+ * faults, traps or hangs. No counterpart in the reference.
+ */
+FLASH_PROLOGUE_API int flash_prologue_selftest_wait_timeout(uint32_t tries, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -301,3 +301,21 @@ def test_bulk_copy_and_register_paths_agree(layout, d):
 def test_no_device_wait_timeouts():
     from flash_attn_prologue_b200 import _lib
     assert _lib.device_error(reset=True) == 0
+
+
+def test_bounded_wait_timeout_is_reported_and_context_survives():
+    """Failure detection on the GPU: a wait that nothing completes gives up after
+    its bound, the host reads the error word, and the next launches are correct."""
+    from flash_attn_prologue_b200 import _lib
+    prepare_backend("cute")
+    _lib.device_error(reset=True)
+    _lib.selftest_wait_timeout(4096)
+    torch.cuda.synchronize()
+    assert _lib.device_error(reset=True) == 1
+    assert _lib.device_error(reset=True) == 0
+    args = _cuda_args(_inputs((2, 4, 33, 64), 64, 4, seed=77))
+    out = qknorm_rope_scale(*args, backend="cute")
+    torch.cuda.synchronize()
+    ref = native_forward(*[t.detach().cpu() for t in args])
+    _check_outputs(out, ref, torch.bfloat16, [t.detach().cpu() for t in args])
+    assert _lib.device_error(reset=True) == 0
