@@ -14,6 +14,7 @@ from .layers.RMSNorm import RMSNormRoPEScale
 __version__ = "0.2.0"
 
 _LAZY = {
+    "qknorm_rope_scale_op": ("epilogue_kernel", "qknorm_rope_scale_op"),
     "qknorm_rope_scale_cute_op": ("fused_epilogue", "qknorm_rope_scale_cute_op"),
     "qknorm_rope_scale_cute_backward_op": ("fused_epilogue", "qknorm_rope_scale_cute_backward_op"),
     "qknorm_rope_scale_cute_inverse_op": ("fused_epilogue", "qknorm_rope_scale_cute_inverse_op"),

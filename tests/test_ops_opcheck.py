@@ -110,3 +110,11 @@ def test_compiled_fused_qkv_epilogue_matches_eager():
     compiled = step(torch.compile(fn, fullgraph=True, dynamic=False))
     for a, b in zip(eager[0] + eager[1], compiled[0] + compiled[1]):
         assert torch.equal(a, b)
+
+
+def test_opcheck_reference_qkv_op():
+    from flash_attn_prologue_b200 import epilogue_kernel  # noqa: F401  (registers the op)
+    B, N, H, D = 2, 24, 4, 64
+    qkv = torch.randn(B, N, 3 * H * D, device="cuda").to(torch.bfloat16).requires_grad_()
+    _, _, w, s, sin, cos = _prologue_args(B, H, N, D)
+    _ok(torch.library.opcheck(OPS.qknorm_rope_scale.default, (qkv, w, s, sin, cos, 1e-5), test_utils=CHECKS))

@@ -87,3 +87,32 @@ def test_cute_gradient_equals_gathered_slice_gradients(shape, use_v):
         assert a.shape == b.shape and torch.equal(a, b)
     if gv is None:
         assert float(got[0][..., 2, :, :].abs().max()) == 0.0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("weight_2d", [False, True])
+def test_reference_qkv_op_matches_slice_path(weight_2d):
+    """flash_prologue::qknorm_rope_scale on [B, N, 3*H*D] (reference epilogue_kernel.py:247-369):
+    outputs and gradients equal to the frontend on the slices (the same kernels)."""
+    B, N, H, D = 2, 40, 4, 64
+    g = torch.Generator(device="cuda").manual_seed(8)
+    qkv = torch.randn(B, N, 3 * H * D, generator=g, device="cuda").to(torch.bfloat16)
+    w = 1 + 0.1 * torch.randn(2, 1, D, generator=g, device="cuda")
+    s = 0.1 * torch.randn(H, 1, 1, generator=g, device="cuda")
+    ang = torch.rand(N, D // 2, generator=g, device="cuda") * 3
+    sin, cos = ang.sin()[None, None], ang.cos()[None, None]
+    gq, gk, gv = (torch.randn(B, H, N, D, generator=g, device="cuda").to(torch.bfloat16) for _ in range(3))
+    x = qkv.detach().clone().requires_grad_()
+    wl = (w[:, 0] if weight_2d else w).detach().clone().requires_grad_()
+    sl = s.detach().clone().requires_grad_()
+    q, k, v = fap.qknorm_rope_scale_op(x, wl, sl, sin, cos, 1e-5)
+    assert q.is_contiguous() and v.is_contiguous() and q.shape == (B, H, N, D)
+    got = torch.autograd.grad((q, k, v), (x, wl, sl), (gq, gk, gv))
+    xr = qkv.detach().clone().requires_grad_()
+    wr, sr = w.detach().clone().requires_grad_(), s.detach().clone().requires_grad_()
+    qs, ks, vs = xr.view(B, N, 3, H, D).unbind(2)
+    rq, rk = fap.qknorm_rope_scale(qs.transpose(1, 2), ks.transpose(1, 2), wr, sr, sin, cos, backend="cute")
+    ref = torch.autograd.grad((rq, rk, vs.transpose(1, 2)), (xr, wr, sr), (gq, gk, gv))
+    assert torch.equal(q, rq) and torch.equal(k, rk) and torch.equal(v, vs.transpose(1, 2))
+    assert torch.equal(got[0], ref[0])
+    assert torch.equal(got[1], ref[1].reshape(got[1].shape)) and torch.equal(got[2], ref[2])
