@@ -685,33 +685,55 @@ int resident_pairs(const cudaLaunchConfig_t& cfg) {
   return n;
 }
 
+// Launch configuration of a pair kernel (grid set by the caller) and the
+// number of its 2-CTA clusters that can be resident at once (0 if none can:
+// the single-CTA mainloop is used then).
 template <int D, int EPI>
-cudaError_t launch_pair(const CUtensorMap& mx, const CUtensorMap& mw, const OutMaps& om,
-                        const GemmArgs& args, cudaStream_t stream) {
+int pair_config(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, cudaStream_t stream) {
   using C = PairConfig<EPI>;
   const size_t smem = smem_bytes_for(C::kStages, kStageBytesPair, kStagingBufsPair, EPI, D);
-  cudaError_t err = cudaFuncSetAttribute(qkv_gemm_pair_kernel<D, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (err != cudaSuccess) return err;
+  if (cudaFuncSetAttribute(qkv_gemm_pair_kernel<D, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return 0;
   const int sms = sm_count();
-  if (sms <= 0) return cudaErrorInvalidDevice;
-  cudaLaunchAttribute attr[1];
+  if (sms < 2) return 0;
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(sms & ~1));
-  cfg.blockDim = dim3(C::R::kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const int pairs_max = resident_pairs<D, EPI>(cfg);
+  *cfg = cudaLaunchConfig_t{};
+  cfg->gridDim = dim3((unsigned)(sms & ~1));
+  cfg->blockDim = dim3(C::R::kThreads);
+  cfg->dynamicSmemBytes = smem;
+  cfg->stream = stream;
+  cfg->attrs = attr;
+  cfg->numAttrs = 1;
+  const int n = resident_pairs<D, EPI>(*cfg);
+  return n > 0 ? n : 0;
+}
+
+template <int D, int EPI>
+cudaError_t launch_pair(const CUtensorMap& mx, const CUtensorMap& mw, const OutMaps& om,
+                        const GemmArgs& args, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[1];
+  const int pairs_max = pair_config<D, EPI>(&cfg, attr, stream);
   if (pairs_max <= 0) return cudaErrorInvalidConfiguration;
   const int64_t pairs = args.n_tiles < pairs_max ? args.n_tiles : pairs_max;
   cfg.gridDim = dim3((unsigned)(2 * pairs));
   return cudaLaunchKernelEx(&cfg, qkv_gemm_pair_kernel<D, EPI>, mx, mw, om, args);
+}
+
+// Which pair kernel serves this call (8 epilogue warps for the D = 128
+// prologue: at D = 64 the 168-register budget of 10 warps would spill), and
+// whether it can run here at all.
+int pair_epilogue_warps(int64_t D, int apply_prologue) { return (apply_prologue && D == 128) ? 8 : 4; }
+
+bool pair_runnable(int64_t D, int apply_prologue, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[1];
+  if (pair_epilogue_warps(D, apply_prologue) == 8) return pair_config<128, 8>(&cfg, attr, stream) > 0;
+  return (D == 64 ? pair_config<64, 4>(&cfg, attr, stream) : pair_config<128, 4>(&cfg, attr, stream)) > 0;
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -765,7 +787,9 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(
         ((sin_strides[0] | sin_strides[1] | cos_strides[0] | cos_strides[1]) & 3) != 0)
       return FLASH_PROLOGUE_ERR_ALIGNMENT;
   }
-  const bool pair = g_gemm_variant == 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // CTA pairs unless selected off or the device cannot co-schedule 2-CTA clusters.
+  const bool pair = g_gemm_variant == 0 && pair_runnable(D, apply_prologue, s);
   const int rows = pair ? kRowsPair : kRowsSingle;
   // Per CTA the pair loads 128 rows of X and 128 of W per stage; the single
   // CTA 128 rows of X and 256 of W.
@@ -796,11 +820,8 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(
   } else {
     for (int i = 0; i < 5; ++i) om.m[i] = mx;  // unused
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t err;
-  // Pair configurations: 8 epilogue warps for the D = 128 prologue (at D = 64
-  // the 168-register budget of 10 warps would spill), 4 otherwise.
-  if (pair && apply_prologue && D == 128)
+  if (pair && pair_epilogue_warps(D, apply_prologue) == 8)
     err = launch_pair<128, 8>(mx, mw, om, g, s);
   else if (pair)
     err = (D == 64) ? launch_pair<64, 4>(mx, mw, om, g, s) : launch_pair<128, 4>(mx, mw, om, g, s);

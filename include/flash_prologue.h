@@ -208,7 +208,9 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(const void* x, const void* w,
  * Mainloop of flash_prologue_qkv_gemm_fwd (process-wide, not thread-safe; for
  * tests and tuning). 0 (default): CTA pairs -- 2-CTA clusters running
  * tcgen05.mma.cta_group::2 on 256 x 256 tiles, each CTA loading half of the
- * operands; 1: one CTA per SM on 128 x 256 tiles. Both give identical results.
+ * operands (the single-CTA mainloop is used instead where the device cannot
+ * co-schedule 2-CTA clusters); 1: one CTA per SM on 128 x 256 tiles. Both
+ * give identical results.
  * No counterpart in the reference (whose GEMM is a CuTe-DSL sm_120a kernel,
  * fused_qkv.py:25, 53-594).
  */
