@@ -1,6 +1,6 @@
 """Builds libflash_prologue.so (the C-ABI library) in-tree with nvcc for sm_100a.
 
-Usage: python -m flash_attn_prologue_b200.build [--force] [--debug]
+Usage: python -m flash_attn_prologue_b200.build [--force] [-j JOBS]
 
 Each csrc/*.cu compiles to an object under _build/ (in parallel), then the
 objects link into flash_attn_prologue_b200/libflash_prologue.so. A source is
@@ -47,9 +47,9 @@ def _compile(src: Path, obj: Path, extra, log_dir: Path):
     return obj
 
 
-def build(force: bool = False, debug: bool = False, jobs: int = 0) -> Path:
+def build(force: bool = False, jobs: int = 0) -> Path:
     BUILD.mkdir(exist_ok=True)
-    extra = ["-DFLASH_PROLOGUE_DEBUG=1"] if debug else []
+    extra = []
     deps = _deps_mtime()
     srcs = sorted(CSRC.glob("*.cu"))
     todo = []
@@ -76,10 +76,9 @@ def build(force: bool = False, debug: bool = False, jobs: int = 0) -> Path:
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--force", action="store_true")
-    ap.add_argument("--debug", action="store_true")
     ap.add_argument("-j", "--jobs", type=int, default=0)
     args = ap.parse_args(argv)
-    lib = build(force=args.force, debug=args.debug, jobs=args.jobs)
+    lib = build(force=args.force, jobs=args.jobs)
     print(lib)
 
 
