@@ -52,6 +52,20 @@ constexpr int kTmaConsumerWarps = 8;                       // 0-3: Q rows, 4-7: 
 constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kTmaTileBytes = 8192;                        // per streamed tensor per stage
 
+// The backward kernel runs the 8 consumer warps (warpgroups 0-1) beside a
+// whole producer warpgroup (warp 8 issues the copies; warps 9-11 leave once
+// the group has given its registers back). It is launched at
+// kTmaBwdLaunchRegs registers per thread (two CTAs per SM: 2 x 384 x 80 fit in
+// the 65,536-register file); the producer group then drops to 32 and the
+// consumers rise to 104, which the block's own allocation covers exactly.
+constexpr int kTmaBwdThreads = (kTmaConsumerWarps + 4) * 32;
+constexpr int kTmaBwdLaunchRegs = 80;
+constexpr int kTmaBwdProducerRegs = 32;
+constexpr int kTmaBwdConsumerRegs = 104;
+static_assert(4 * 32 * kTmaBwdProducerRegs + kTmaConsumerWarps * 32 * kTmaBwdConsumerRegs <=
+                  kTmaBwdThreads * kTmaBwdLaunchRegs,
+              "backward register split exceeds the block's launch allocation");
+
 struct TmaPlan {
   int heads_inner;      // inner row dim: 1 = heads, 0 = positions
   int ti, log2_ti;      // rows per tile along the inner dim (power of two)

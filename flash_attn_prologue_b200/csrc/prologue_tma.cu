@@ -16,6 +16,9 @@
 // The arithmetic per row is the one of the register-path kernels
 // (prologue_fwd.cu / prologue_bwd.cu), in the same order, so both paths give
 // bit-identical results.
+#include <mutex>
+#include <unordered_set>
+
 #include "prologue_host.h"
 #include "tma_util.cuh"
 
@@ -243,7 +246,7 @@ __device__ __forceinline__ float load_saved_r(const TmaBwdArgs& a, const TileCoo
 }
 
 template <typename T, int D, bool INV>
-__global__ void __launch_bounds__(kTmaThreads, 2)
+__global__ void __launch_bounds__(kTmaBwdThreads, 2)
     prologue_bwd_tma_kernel(const __grid_constant__ TmaBwdArgs a) {
   using S_ = TmaShape<T, D>;
   constexpr int HALF = S_::HALF;
@@ -269,19 +272,21 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     }
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < 2 * D; i += kTmaThreads) w_s[i] = a.w[i];
-  for (int i = threadIdx.x; i < a.H; i += kTmaThreads) e_s[i] = (float)exp((double)a.scales[i]);
-  for (int i = threadIdx.x; i < 4 * a.H; i += kTmaThreads) ds_s[i] = 0.f;
+  for (int i = threadIdx.x; i < 2 * D; i += kTmaBwdThreads) w_s[i] = a.w[i];
+  for (int i = threadIdx.x; i < a.H; i += kTmaBwdThreads) e_s[i] = (float)exp((double)a.scales[i]);
+  for (int i = threadIdx.x; i < 4 * a.H; i += kTmaBwdThreads) ds_s[i] = 0.f;
   if constexpr (INV) {
-    for (int i = threadIdx.x; i < 2 * D; i += kTmaThreads) iw_s[i] = __frcp_rn(a.w[i]);
-    for (int i = threadIdx.x; i < a.H; i += kTmaThreads) ie_s[i] = (float)(1.0 / exp((double)a.scales[i]));
+    for (int i = threadIdx.x; i < 2 * D; i += kTmaBwdThreads) iw_s[i] = __frcp_rn(a.w[i]);
+    for (int i = threadIdx.x; i < a.H; i += kTmaBwdThreads) ie_s[i] = (float)(1.0 / exp((double)a.scales[i]));
   }
   __syncthreads();
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   Cursor4 cur;
-  if (warp == kTmaConsumerWarps) {  // ---------------- producer ----------------
+  if (warp >= kTmaConsumerWarps) {  // ---------------- producer warpgroup ----------------
+    setmaxnreg_dec<kTmaBwdProducerRegs>();
+    if (warp != kTmaConsumerWarps) return;
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_table = policy_evict_last();
     int k = 0;
@@ -299,6 +304,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   }
 
   // ---------------- consumers: warps 0-3 Q, warps 4-7 K ----------------
+  setmaxnreg_inc<kTmaBwdConsumerRegs>();
   const int t = warp >> 2;
   const int gtid = threadIdx.x & (S_::GROUP_THREADS - 1);
   const int c = gtid & (L - 1);
@@ -532,12 +538,32 @@ static cudaError_t prepare_kernel(const void* fn, size_t smem) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 
+// The backward kernel's register split (producer warpgroup down, consumers up)
+// only completes if the kernel was built with at least kTmaBwdLaunchRegs
+// registers per thread; a build with fewer is refused here instead of launched.
+static cudaError_t check_bwd_registers(const void* fn) {
+  static std::mutex mu;
+  static std::unordered_set<const void*> checked;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (checked.count(fn)) return cudaSuccess;
+  }
+  cudaFuncAttributes attr;
+  cudaError_t err = cudaFuncGetAttributes(&attr, fn);
+  if (err != cudaSuccess) return err;
+  if (attr.numRegs < kTmaBwdLaunchRegs) return cudaErrorInvalidConfiguration;
+  std::lock_guard<std::mutex> lock(mu);
+  checked.insert(fn);
+  return cudaSuccess;
+}
+
 int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype, bool inv) {
   const void* fn = tma_kernel_for(bwd, dtype, D, inv);
   if (!fn) return -1;
   const size_t smem = tma_smem_bytes(p, D, bwd ? 4 : 2, H, inv);
   if (prepare_kernel(fn, smem) != cudaSuccess) return -1;
-  return persistent_grid(fn, smem, p.n_tiles, kTmaThreads);
+  if (bwd && check_bwd_registers(fn) != cudaSuccess) return -1;
+  return persistent_grid(fn, smem, p.n_tiles, bwd ? kTmaBwdThreads : kTmaThreads);
 }
 
 cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream) {
@@ -561,12 +587,14 @@ cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype,
   const size_t smem = tma_smem_bytes(a.p, D, 4, a.H, inv);
   cudaError_t err = prepare_kernel(fn, smem);
   if (err != cudaSuccess) return err;
-  const int64_t grid = persistent_grid(fn, smem, a.p.n_tiles, kTmaThreads);
+  err = check_bwd_registers(fn);
+  if (err != cudaSuccess) return err;
+  const int64_t grid = persistent_grid(fn, smem, a.p.n_tiles, kTmaBwdThreads);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
   TmaBwdArgs launch_args = a;
   launch_args.p.radix = make_radix(a.p.n_ib, a.p.n_ob, a.B, grid);
   void* args[] = {&launch_args};
-  err = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kTmaThreads), args, smem, stream);
+  err = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kTmaBwdThreads), args, smem, stream);
   if (err != cudaSuccess) return err;
   return launch_bwd_finalize(a.partials, grid, 2 * D + a.H, 2 * D, dw, ds, stream);
 }

@@ -82,6 +82,18 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Warpgroup register reallocation: all 128 threads of a warpgroup execute the
+// same instruction. An increase waits until the block's pool (registers per
+// thread at launch x threads) has room, so the split must fit that pool.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Barrier over the consumer warps only (the producer warp does not take part).
 __device__ __forceinline__ void consumer_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
