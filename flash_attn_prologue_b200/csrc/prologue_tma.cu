@@ -1,6 +1,8 @@
 // Bulk-copy (TMA) pipelined forward and backward prologue kernels.
 //
-// CTA = 8 consumer warps + 1 producer warp, two CTAs per SM. A tile is a block
+// CTA = 8 consumer warps + 1 producer warp, two CTAs per SM (the backward CTA
+// has a whole producer warpgroup, which hands its registers to the consumers:
+// kTmaBwdThreads in prologue_host.h). A tile is a block
 // of rows of one batch b: `ti` consecutive rows along the "inner" row dim
 // (heads for packed [T,H,D] views, positions for dense [B,H,N,D]), whose rows
 // are contiguous in memory (inner stride == D), times `to` indices of the outer
