@@ -566,6 +566,22 @@ def run_c5_profile_case(T):
         raise SystemExit("device error word set")
 
 
+def run_c5_bwd_profile_case(T):
+    """Three calls of the projection backward (dX and dW GEMM kernels) at C5's hidden size and heads."""
+    import flash_attn_prologue_b200 as fap
+    from flash_attn_prologue_b200 import _lib
+    hidden, H, D = 2048, 16, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(1, T, hidden, generator=g, device="cuda").to(torch.bfloat16)
+    wq = (0.02 * torch.randn(3 * H * D, hidden, generator=g, device="cuda")).to(torch.bfloat16)
+    gq, gk, gv = (torch.randn(1, H, T, D, generator=g, device="cuda").to(torch.bfloat16) for _ in range(3))
+    for _ in range(3):
+        fap.fused_qkv_backward(gq, gk, gv, wq, x)
+    torch.cuda.synchronize()
+    if _lib.device_error(reset=True) != 0:
+        raise SystemExit("device error word set")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -582,11 +598,17 @@ def main():
     ap.add_argument("--c5-profile-tokens", type=int, default=0,
                     help="only run the fused QKV GEMM + prologue (C5 shapes, this many tokens) three "
                          "times and exit: the small case an ncu capture of that kernel uses")
+    ap.add_argument("--c5-bwd-profile-tokens", type=int, default=0,
+                    help="only run the projection backward GEMMs (C5 shapes, this many tokens) three "
+                         "times: the case the backward GEMM ncu captures use")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.c5_profile_tokens:
         run_c5_profile_case(args.c5_profile_tokens)
+        return
+    if args.c5_bwd_profile_tokens:
+        run_c5_bwd_profile_case(args.c5_bwd_profile_tokens)
         return
     if args.impl == "reference":
         # The reference path is CPU code: rank 0 runs it, other ranks exit at once.

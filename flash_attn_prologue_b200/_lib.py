@@ -53,6 +53,13 @@ SIGNATURES = {
     "flash_prologue_qkv_gemm_fwd": ([_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp,
                                      _vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _vp, _vp,
                                      ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
+    "flash_prologue_qkv_bwd_dx": ([_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
+                                   _i64, _i64, _i64, _i64, _i64, _vp], ctypes.c_int),
+    "flash_prologue_qkv_bwd_dw_workspace_size": ([_i64, _i64, _i64, _i64, _i64,
+                                                  ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "flash_prologue_qkv_bwd_dw": ([_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp, ctypes.c_int,
+                                   _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64, _i64, _vp],
+                                  ctypes.c_int),
     "flash_prologue_set_path": ([ctypes.c_int], ctypes.c_int),
     "flash_prologue_set_gemm_variant": ([ctypes.c_int], ctypes.c_int),
     "flash_prologue_selftest_wait_timeout": ([ctypes.c_uint32, _vp], ctypes.c_int),

@@ -227,11 +227,12 @@ extern "C" {
 
 FLASH_PROLOGUE_API int flash_prologue_device_error(int* value, int reset) {
   if (!value) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   if (read_device_error(&a, reset != 0) != cudaSuccess ||
-      read_gemm_device_error(&b, reset != 0) != cudaSuccess)
+      read_gemm_device_error(&b, reset != 0) != cudaSuccess ||
+      read_gemm_bwd_device_error(&c, reset != 0) != cudaSuccess)
     return FLASH_PROLOGUE_ERR_CUDA;
-  *value = a | b;
+  *value = a | b | c;
   return FLASH_PROLOGUE_OK;
 }
 

@@ -119,9 +119,10 @@ struct TmaBwdArgs {
 TmaPlan plan_tma(int64_t B, int64_t H, int64_t N, int D, int dtype, bool heads_inner, int stages);
 size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv = false);
 // Read (synchronously) and optionally clear the error words of the bulk-copy
-// prologue kernels and of the fused QKV GEMM.
+// prologue kernels, of the fused QKV GEMM and of its backward GEMMs.
 cudaError_t read_device_error(int* value, bool reset);
 cudaError_t read_gemm_device_error(int* value, bool reset);
+cudaError_t read_gemm_bwd_device_error(int* value, bool reset);
 // One thread waits (bounded by `tries` polls) on a barrier nothing arrives at.
 cudaError_t launch_selftest_wait_timeout(uint32_t tries, cudaStream_t stream);
 int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype, bool inv = false);

@@ -54,6 +54,23 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// The same for an MN-major operand tile (the backward GEMMs' transposed
+// operands): TMA boxes of 64 MN-elements (128 bytes) x 64 K-rows, 128-byte
+// swizzle, so a swizzle atom is 8 K-rows x 64 MN-elements (1024 bytes). The
+// canonical MN-major layout ((8,n),(8,k)) : ((1,LBO),(8,SBO)) in 16-byte
+// units: LBO = bytes between 64-element blocks along MN (one box, `lbo`),
+// SBO = bytes between 8-row groups along K (1024). One K = 16 step of an MMA
+// advances the start address by two atoms (2048 bytes).
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t smem_addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
 // Instruction descriptor of tcgen05.mma kind::f16: BF16 A and B, FP32
 // accumulator, both operands K-major, shape M x N (bits: D format 4-5,
 // A format 7-9, B format 10-12, A/B major 15/16, N >> 3 at 17-22, M >> 4 at 24-28).
@@ -63,6 +80,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          | (1u << 10)                     // B: BF16
          | ((uint32_t)(N >> 3) << 17)
          | ((uint32_t)(M >> 4) << 24);
+}
+
+// With A and/or B MN-major (bits 15 and 16 of the instruction descriptor).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_major(int M, int N, bool a_mn, bool b_mn) {
+  return idesc_bf16_f32(M, N) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
@@ -261,6 +283,48 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];"
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+// 3-D and 4-D forms of tma_load_2d_pair (innermost coordinate first; the
+// same alignment rule on c0).
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int32_t c0,
+                                                 int32_t c1, int32_t c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+        "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, int32_t c0,
+                                                 int32_t c1, int32_t c2, int32_t c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+        "r"(c3), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d_pair(void* dst, const CUtensorMap* map, int32_t c0,
+                                                 int32_t c1, int32_t c2, int32_t c3, int32_t c4,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+        "r"(c3), "r"(c4), "r"(bar)
+      : "memory");
+}
+
+// 3-D tiled TMA store from shared memory (bulk-group completion; coordinates
+// non-negative, rows outside the tensor not written).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int32_t c0, int32_t c1,
+                                             int32_t c2, const void* src) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];"
+      ::"l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
       : "memory");
 }
 

@@ -15,15 +15,16 @@ Custom ops under the reference's names (flash_attn_prologue/fused_qkv.py):
 * the projection backward ops ``fused_qkv_backward``, ``matmul_bwd_dx_cute``,
   ``matmul_bwd_dw_cute``, ``matmul_bwd_dw_accumulate_cute`` and the Python
   ``matmul_bwd_dx`` / ``matmul_bwd_dw`` (reference: gemm_bwd.py:1171-1566),
-  as one gather of dP plus library GEMMs.
+  as two tcgen05 GEMM kernels (csrc/qkv_gemm_bwd.cu) that read the per-head
+  gradients in place.
 
 ``weight`` is the nn.Linear weight ``[3*H*D, hidden]`` with rows Q heads | K
 heads | V heads; D is taken from ``rmsnorm_weight`` (the reference hard-codes
 64, fused_qkv.py:606-607); H = weight.shape[0] // (3 * D). The projection is
 rounded to BF16 before the prologue, as a BF16 linear layer followed by the
 prologue would do. Backward: the prologue backward kernel on the saved
-(or recomputed) projections writing dq, dk straight into the dP operand
-buffer, then dX = dP @ W and dW = dP^T @ X as plain library GEMMs.
+(or recomputed) projections, then dX = dP @ W and dW = dP^T @ X by the
+backward GEMM kernels reading dq, dk, dv in place as the head blocks of dP.
 """
 from typing import Optional, Tuple
 
@@ -115,18 +116,77 @@ def _fused_qkv_fake(x, weight):
                  for _ in range(3))
 
 
-def _gather_dp(dq, dk, dv):
-    """dP [B*N, 3*H*D] (the gradient of x @ weight.T) from per-head [B, H, N, D] gradients, one pass."""
-    B, H, N, D = dq.shape
-    dp = torch.empty((B, N, 3, H, D), dtype=dq.dtype, device=dq.device)
-    for slot, g in enumerate((dq, dk, dv)):
-        dp[:, :, slot].copy_(g.transpose(1, 2))
-    return dp.view(B * N, 3 * H * D)
-
-
 def _check_grads_qkv(grad_q, grad_k, grad_v):
     if grad_q.ndim != 4 or grad_k.shape != grad_q.shape or grad_v.shape != grad_q.shape:
         raise ValueError("grad_q/grad_k/grad_v must be matching [B, H, N, D] tensors")
+
+
+def _tma_view(g: torch.Tensor) -> torch.Tensor:
+    """g itself when the backward GEMMs can read it in place (BF16, d contiguous,
+    16-byte aligned base and row strides), else a contiguous copy."""
+    if g.dtype != torch.bfloat16:
+        raise ValueError("the projection backward takes BF16 gradients")
+    st = g.stride()
+    ok = (st[3] == 1 and g.data_ptr() % 16 == 0 and
+          all(st[i] % 8 == 0 and st[i] > 0 for i in range(3) if g.shape[i] > 1))
+    return g if ok else g.contiguous()
+
+
+def _check_bwd_shapes(B, H, N, D, hidden, device):
+    if device.type != "cuda":
+        raise ValueError("the projection backward GEMMs run on CUDA devices only")
+    if D not in (64, 128) or (H * D) % BN_TILE or hidden % 64:
+        raise ValueError("the projection backward needs D in (64, 128), H * D a multiple of 256 "
+                         "and hidden a multiple of 64")
+
+
+def _bwd_dx(dq, dk, dv, weight):
+    """dX [B, N, hidden] = dP @ weight, dP read from the [B, H, N, D] gradients in place."""
+    B, H, N, D = dq.shape
+    hidden = int(weight.shape[1])
+    _check_bwd_shapes(B, H, N, D, hidden, dq.device)
+    if weight.dtype != torch.bfloat16 or tuple(weight.shape) != (3 * H * D, hidden):
+        raise ValueError("weight must be BF16 [3*H*D, hidden]")
+    w = weight.contiguous()
+    views = [_tma_view(g) for g in (dq, dk, dv)]
+    grad_x = torch.empty((B, N, hidden), dtype=torch.bfloat16, device=dq.device)
+    with _DeviceGuard(dq.device):
+        status = _lib.load().flash_prologue_qkv_bwd_dx(
+            _lib.ptr(views[0]), _lib.strides4(views[0]), _lib.ptr(views[1]), _lib.strides4(views[1]),
+            _lib.ptr(views[2]), _lib.strides4(views[2]), _lib.ptr(w), _lib.ptr(grad_x),
+            B, H, N, D, hidden, _lib.stream_of(dq.device))
+    _lib.check(status, "flash_prologue_qkv_bwd_dx")
+    return grad_x
+
+
+def _bwd_dw(dq, dk, dv, x, out=None):
+    """dW [3*H*D, hidden] = dP^T @ x (or added to ``out``), dP read in place."""
+    B, H, N, D = dq.shape
+    hidden = int(x.shape[-1])
+    _check_bwd_shapes(B, H, N, D, hidden, dq.device)
+    if x.dtype != torch.bfloat16 or x.numel() != B * N * hidden:
+        raise ValueError("x must be BF16 [B, N, hidden]")
+    x3 = x.reshape(B, N, hidden).contiguous()
+    views = [_tma_view(g) for g in (dq, dk, dv)]
+    grad_w = out if out is not None else torch.empty((3 * H * D, hidden), dtype=torch.bfloat16,
+                                                      device=dq.device)
+    if out is not None and (out.dtype != torch.bfloat16 or tuple(out.shape) != (3 * H * D, hidden)
+                            or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous BF16 [3*H*D, hidden] tensor")
+    lib = _lib.load()
+    with _DeviceGuard(dq.device):
+        nbytes = _lib.ctypes.c_size_t(0)
+        _lib.check(lib.flash_prologue_qkv_bwd_dw_workspace_size(B, H, N, D, hidden,
+                                                                _lib.ctypes.byref(nbytes)),
+                   "flash_prologue_qkv_bwd_dw_workspace_size")
+        ws = torch.empty(max(int(nbytes.value), 16), dtype=torch.uint8, device=dq.device)
+        status = lib.flash_prologue_qkv_bwd_dw(
+            _lib.ptr(views[0]), _lib.strides4(views[0]), _lib.ptr(views[1]), _lib.strides4(views[1]),
+            _lib.ptr(views[2]), _lib.strides4(views[2]), _lib.ptr(x3), _lib.ptr(grad_w),
+            1 if out is not None else 0, _lib.ptr(ws), int(nbytes.value), B, H, N, D, hidden,
+            _lib.stream_of(dq.device))
+    _lib.check(status, "flash_prologue_qkv_bwd_dw")
+    return grad_w
 
 
 @torch.library.custom_op("flash_prologue::matmul_bwd_dx_cute", mutates_args=())
@@ -137,7 +197,7 @@ def matmul_bwd_dx(grad_q: torch.Tensor, grad_k: torch.Tensor, grad_v: torch.Tens
     B, H, N, D = grad_q.shape
     if grad_q.numel() == 0 or weight.numel() == 0:
         return torch.zeros((B * N, weight.shape[1]), dtype=grad_q.dtype, device=grad_q.device)
-    return _gather_dp(grad_q, grad_k, grad_v) @ weight
+    return _bwd_dx(grad_q, grad_k, grad_v, weight).view(B * N, weight.shape[1])
 
 
 @matmul_bwd_dx.register_fake
@@ -155,7 +215,7 @@ def _matmul_bwd_dw_op(grad_q: torch.Tensor, grad_k: torch.Tensor, grad_v: torch.
     hidden = x.shape[-1]
     if grad_q.numel() == 0 or x.numel() == 0:
         return torch.zeros((3 * H * D, hidden), dtype=grad_q.dtype, device=grad_q.device)
-    return _gather_dp(grad_q, grad_k, grad_v).t() @ x.reshape(B * N, hidden)
+    return _bwd_dw(grad_q, grad_k, grad_v, x)
 
 
 @_matmul_bwd_dw_op.register_fake
@@ -169,10 +229,9 @@ def _matmul_bwd_dw_accumulate_op(grad_q: torch.Tensor, grad_k: torch.Tensor, gra
                                  x: torch.Tensor, out: torch.Tensor) -> None:
     """out += dP^T @ X in place (reference: gemm_bwd.py:1341-1421)."""
     _check_grads_qkv(grad_q, grad_k, grad_v)
-    B, H, N, D = grad_q.shape
     if grad_q.numel() == 0 or x.numel() == 0:
         return
-    out.addmm_(_gather_dp(grad_q, grad_k, grad_v).t(), x.reshape(B * N, x.shape[-1]))
+    _bwd_dw(grad_q, grad_k, grad_v, x, out=out)
 
 
 @_matmul_bwd_dw_accumulate_op.register_fake
@@ -188,11 +247,9 @@ def matmul_bwd_dw(grad_q, grad_k, grad_v, x, out=None):
     return out
 
 
-def _linear_backward_from_dp(dp, weight, x):
-    B, N = x.shape[0], x.shape[1]
-    grad_x = (dp @ weight).reshape(B, N, weight.shape[1])
-    grad_w = dp.t() @ x.reshape(B * N, -1)
-    return grad_x, grad_w
+def _slot_views(dp5):
+    """The q, k, v gradient views [B, H, N, D] of a packed [B, N, 3, H, D] dP."""
+    return [dp5[:, :, i].permute(0, 2, 1, 3) for i in range(3)]
 
 
 @torch.library.custom_op("flash_prologue::fused_qkv_backward", mutates_args=())
@@ -200,8 +257,8 @@ def fused_qkv_backward(grad_q: torch.Tensor, grad_k: torch.Tensor, grad_v: torch
                        weight: torch.Tensor, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """(grad_x [B, N, hidden], grad_weight [3*H*D, hidden]) of P = x @ weight.T split into heads.
 
-    Reference: gemm_bwd.py:1440-1552 (hand-written mma.sync GEMMs there; here
-    one gather of dP and two library GEMMs). Empty inputs give zeros.
+    Reference: gemm_bwd.py:1440-1552. Here two tcgen05 GEMM kernels read the
+    three gradients in place (no gather of dP). Empty inputs give zeros.
     """
     _check_grads_qkv(grad_q, grad_k, grad_v)
     B, H, N, D = grad_q.shape
@@ -209,7 +266,7 @@ def fused_qkv_backward(grad_q: torch.Tensor, grad_k: torch.Tensor, grad_v: torch
     if grad_q.numel() == 0 or x.numel() == 0 or weight.numel() == 0:
         return (torch.zeros((B, N, hidden), dtype=grad_q.dtype, device=grad_q.device),
                 torch.zeros((3 * H * D, hidden), dtype=grad_q.dtype, device=grad_q.device))
-    return _linear_backward_from_dp(_gather_dp(grad_q, grad_k, grad_v), weight, x)
+    return _bwd_dx(grad_q, grad_k, grad_v, weight), _bwd_dw(grad_q, grad_k, grad_v, x)
 
 
 @fused_qkv_backward.register_fake
@@ -266,25 +323,22 @@ def _prologue_and_linear_backward(x, weight, rmsnorm_weight, scales, sin, cos, q
                                   grad_q, grad_k, grad_v, eps=1e-5):
     """(grad_x, grad_w, dw, ds) of the fused projection + prologue.
 
-    The prologue backward kernel writes dq and dk straight into the Q and K
-    slots of dP [B, N, 3, H, D] (the gradient of x @ weight.T, laid out so
-    that it is the [B*N, 3*H*D] GEMM operand with no gather); dv goes into the
-    V slot; then dX = dP @ W and dW = dP^T @ X as library GEMMs.
+    The prologue backward kernel writes dq and dk into a [B, N, 2, H, D]
+    buffer; the backward GEMM kernels then read dq, dk and the upstream dv in
+    place as the three head blocks of dP (dX = dP @ W, dW = dP^T @ X).
     """
     B, H, N, D = q_proj.shape
-    dp5 = torch.empty((B, N, 3, H, D), dtype=q_proj.dtype, device=q_proj.device)
+    dqk = torch.empty((B, N, 2, H, D), dtype=q_proj.dtype, device=q_proj.device)
+    dq = dqk[:, :, 0].permute(0, 2, 1, 3)
+    dk = dqk[:, :, 1].permute(0, 2, 1, 3)
     sin4 = _ensure_4d(sin).expand(B, 1, N, D // 2)
     cos4 = _ensure_4d(cos).expand(B, 1, N, D // 2)
     dw, ds = backward_into(q_proj, k_proj, rmsnorm_weight, scales, sin4, cos4, grad_q, grad_k,
-                           dp5[:, :, 0].permute(0, 2, 1, 3), dp5[:, :, 1].permute(0, 2, 1, 3), eps)
-    if grad_v is None:
-        dp5[:, :, 2].zero_()
-    else:
-        dp5[:, :, 2].copy_(grad_v.transpose(1, 2))
+                           dq, dk, eps)
     if B * N == 0:
         return (torch.zeros_like(x), torch.zeros_like(weight), dw, ds)
-    grad_x, grad_w = _linear_backward_from_dp(dp5.view(B * N, 3 * H * D), weight, x)
-    return grad_x, grad_w, dw, ds
+    dv = torch.zeros_like(q_proj) if grad_v is None else grad_v
+    return _bwd_dx(dq, dk, dv, weight), _bwd_dw(dq, dk, dv, x), dw, ds
 
 
 @torch.library.custom_op("flash_prologue::fused_qkv_epilogue_backward", mutates_args=())

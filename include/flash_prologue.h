@@ -205,6 +205,51 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_gemm_fwd(const void* x, const void* w,
                        float eps, int apply_prologue, void* stream);
 
 /*
+ * Backward of the QKV projection P = x * w^T with P split into heads
+ * (s = q, k, v): grad_x[b, n, :] = sum_{s,h,d} grad_s[b,h,n,d] * w[(s*H+h)*D+d, :].
+ * grad_q/grad_k/grad_v are BF16 [B, H, N, D] views given by element strides
+ * (b, h, n, d) with d stride 1 and the others multiples of 8 (a packed
+ * [B, N, 3, H, D] gradient is three such views); w: [3*H*D, hidden] and
+ * grad_x: [B, N, hidden], both contiguous BF16. tcgen05 GEMM on 2-CTA
+ * clusters reading the gradients in place through TMA (no gather of dP).
+ * Requirements: D in {64, 128}; (H*D) % 256 == 0; hidden % 64 == 0; 16-byte
+ * aligned pointers. Replaces matmul_bwd_dx_cute (flash_attn_prologue/
+ * gemm_bwd.py:1171-1235) and the dX half of fused_qkv_backward
+ * (gemm_bwd.py:1440-1552).
+ */
+FLASH_PROLOGUE_API int flash_prologue_qkv_bwd_dx(const void* grad_q, const int64_t gq_strides[4],
+                       const void* grad_k, const int64_t gk_strides[4],
+                       const void* grad_v, const int64_t gv_strides[4],
+                       const void* w, void* grad_x,
+                       int64_t B, int64_t H, int64_t N, int64_t D, int64_t hidden,
+                       void* stream);
+
+/*
+ * Workspace (FP32 split-reduction partials) flash_prologue_qkv_bwd_dw needs on
+ * the current device for these sizes; 0 when the sum is empty.
+ */
+FLASH_PROLOGUE_API int flash_prologue_qkv_bwd_dw_workspace_size(int64_t B, int64_t H, int64_t N,
+                       int64_t D, int64_t hidden, size_t* bytes);
+
+/*
+ * grad_w[(s*H+h)*D+d, :] = sum_{b,n} grad_s[b,h,n,d] * x[b, n, :] (accumulate
+ * == 0), or added to grad_w (accumulate != 0: the FP32 sum plus the old BF16
+ * value, rounded once). Gradient views as for flash_prologue_qkv_bwd_dx; x:
+ * [B, N, hidden] and grad_w: [3*H*D, hidden], contiguous BF16. The token sum
+ * runs as a tcgen05 GEMM in up to 8 chunks written as FP32 partials to the
+ * workspace and added in chunk order, so results are identical run to run.
+ * Replaces matmul_bwd_dw_cute / matmul_bwd_dw_accumulate_cute
+ * (gemm_bwd.py:1246-1421) and the dW half of fused_qkv_backward.
+ */
+FLASH_PROLOGUE_API int flash_prologue_qkv_bwd_dw(const void* grad_q, const int64_t gq_strides[4],
+                       const void* grad_k, const int64_t gk_strides[4],
+                       const void* grad_v, const int64_t gv_strides[4],
+                       const void* x, void* grad_w, int accumulate,
+                       void* workspace, size_t workspace_bytes,
+                       int64_t B, int64_t H, int64_t N, int64_t D, int64_t hidden,
+                       void* stream);
+
+/*
  * Mainloop of flash_prologue_qkv_gemm_fwd (process-wide, not thread-safe; for
  * tests and tuning). 0 (default): CTA pairs -- 2-CTA clusters running
  * tcgen05.mma.cta_group::2 on 256 x 256 tiles, each CTA loading half of the
