@@ -470,6 +470,28 @@ def run_extras(device, steps=20):
                   "V and the BF16 Q/K projections; gemm_only = the same kernel without the prologue; "
                   "burst fractions against bf16_tflops, sustained against bf16_tflops_sustained")
     out["c5_fused_qkv_gemm"] = c5
+    # C5 projection backward: dX = dP W and dW = dP^T X with dP the per-head
+    # [1, H, T, D] gradients, by the hand-written kernels (read in place) and,
+    # for comparison, by cuBLAS on an already gathered [T, 3HD] dP.
+    gq5, gk5, gv5 = (torch.randn(1, H, T, D, generator=g, device=device).to(torch.bfloat16) for _ in range(3))
+    dp = torch.stack((gq5, gk5, gv5), 0).permute(1, 3, 0, 2, 4).reshape(T, 3 * H * D).contiguous()
+    x2 = x[0]
+    ms = {name: _event_ms(fn, steps) for name, fn in (
+        ("dx", lambda: fap.matmul_bwd_dx(gq5, gk5, gv5, wq)),
+        ("dw", lambda: fap.matmul_bwd_dw(gq5, gk5, gv5, x)),
+        ("cublas_dx_on_gathered_dp", lambda: dp @ wq),
+        ("cublas_dw_on_gathered_dp", lambda: dp.t() @ x2),
+        ("gather_dp", lambda: torch.stack((gq5, gk5, gv5), 0).permute(1, 3, 0, 2, 4).reshape(T, 3 * H * D)
+         .contiguous()))}
+    bwd = {f"{k}_ms": round(v, 4) for k, v in ms.items()}
+    for k in ("dx", "dw"):
+        tf = flop / (ms[k] * 1e-3) / 1e12
+        bwd[f"{k}_tflops"] = round(tf, 1)
+        bwd[f"{k}_frac_of_measured_bf16"] = round(tf / bf16_peak, 4)
+    bwd["note"] = ("dx/dw = tcgen05 GEMM kernels reading the [B, H, N, D] gradients through TMA (no gather); "
+                   "cublas_* = torch matmul on a dP already gathered to [T, 3HD], gather_dp = that gather")
+    out["c5_projection_backward"] = bwd
+    del gq5, gk5, gv5, dp
     return out
 
 
