@@ -57,7 +57,6 @@ constexpr int kMaxSplit = 8;
 enum { kModeDx = 0, kModeDw = 1 };
 
 struct BwdGemmArgs {
-  int mode;
   int split;                 // dW: chunks of the token reduction (1 for dX)
   int64_t B, N, H, D, hidden;
   int64_t tiles_n;           // output tiles along hidden (N fastest)
@@ -525,7 +524,6 @@ int dw_plan(int64_t B, int64_t H, int64_t N, int64_t D, int64_t hidden, cudaStre
   const int pairs = bwd_config<kModeDw>(&cfg, attr, stream);
   if (pairs <= 0) return FLASH_PROLOGUE_ERR_CUDA;
   *a = BwdGemmArgs{};
-  a->mode = kModeDw;
   a->B = B; a->N = N; a->H = H; a->D = D; a->hidden = hidden;
   a->tiles_n = (hidden + kBN - 1) / kBN;
   a->tiles = (3 * H * D / kBN) * a->tiles_n;
@@ -576,7 +574,6 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_bwd_dx(
   const int pairs = bwd_config<kModeDx>(&cfg, attr, s);
   if (pairs <= 0) return FLASH_PROLOGUE_ERR_CUDA;
   BwdGemmArgs a{};
-  a.mode = kModeDx;
   a.split = 1;
   a.B = B; a.N = N; a.H = H; a.D = D; a.hidden = hidden;
   a.m_tiles_per_batch = (N + kBN - 1) / kBN;

@@ -78,6 +78,42 @@ def test_bwd_workspace_size_argument_checks():
     assert lib.flash_prologue_bwd_workspace_size(1, 16, 8, 64, 0, None) == _lib.ERR_INVALID_ARGUMENT
 
 
+def _bwd_dx(B=1, H=4, N=8, D=64, hidden=128, w=16, out=16, null_strides=False):
+    lib = _lib.load()
+    g = ctypes.c_void_p(16)  # never dereferenced: rejected first
+    s4 = None if null_strides else (ctypes.c_int64 * 4)(H * N * D, N * D, D, 1)
+    return lib.flash_prologue_qkv_bwd_dx(g, s4, g, s4, g, s4, w and ctypes.c_void_p(w),
+                                         out and ctypes.c_void_p(out), B, H, N, D, hidden, None)
+
+
+@pytest.mark.parametrize("kwargs,status", [
+    (dict(D=32), _lib.ERR_UNSUPPORTED),
+    (dict(H=3), _lib.ERR_UNSUPPORTED),            # H * D not a multiple of 256
+    (dict(hidden=100), _lib.ERR_UNSUPPORTED),
+    (dict(B=-1), _lib.ERR_INVALID_ARGUMENT),
+    (dict(w=0), _lib.ERR_INVALID_ARGUMENT),
+    (dict(null_strides=True), _lib.ERR_INVALID_ARGUMENT),
+    (dict(w=24), _lib.ERR_ALIGNMENT),
+    (dict(N=0, w=0, out=0), _lib.OK),             # empty sum over no tokens: nothing to write
+])
+def test_projection_backward_argument_checks(kwargs, status):
+    assert _bwd_dx(**kwargs) == status
+
+
+def test_projection_backward_dw_workspace_and_empty_accumulate():
+    lib = _lib.load()
+    n = ctypes.c_size_t(123)
+    assert lib.flash_prologue_qkv_bwd_dw_workspace_size(2, 4, 0, 64, 128, ctypes.byref(n)) == _lib.OK
+    assert n.value == 0
+    assert lib.flash_prologue_qkv_bwd_dw_workspace_size(2, 4, 8, 32, 128, ctypes.byref(n)) == _lib.ERR_UNSUPPORTED
+    assert lib.flash_prologue_qkv_bwd_dw_workspace_size(2, 4, 8, 64, 128, None) == _lib.ERR_INVALID_ARGUMENT
+    s4 = (ctypes.c_int64 * 4)(0, 0, 64, 1)
+    p = ctypes.c_void_p(16)
+    # accumulate into grad_w over zero tokens: leaves it as it is, touches nothing
+    assert lib.flash_prologue_qkv_bwd_dw(p, s4, p, s4, p, s4, p, p, 1, None, 0,
+                                         2, 4, 0, 64, 128, None) == _lib.OK
+
+
 def test_check_maps_status_to_reference_exceptions():
     with pytest.raises(ValueError, match="channel stride"):
         _lib.check(_lib.ERR_CHANNEL_STRIDE, "x")
