@@ -9,6 +9,7 @@ environment variable.
 from importlib import import_module
 
 from .functional import prepare_backend, qknorm_rope_scale, qknorm_rope_scale_qkv
+from .layers.FusedQKV import FusedQKV
 from .layers.RMSNorm import RMSNormRoPEScale
 
 __version__ = "0.2.0"
@@ -27,7 +28,8 @@ _LAZY = {
     "matmul_bwd_dw": ("fused_qkv", "matmul_bwd_dw"),
     "fused_qkv_backward": ("fused_qkv", "fused_qkv_backward"),
 }
-__all__ = ["qknorm_rope_scale", "qknorm_rope_scale_qkv", "prepare_backend", "RMSNormRoPEScale", *_LAZY]
+__all__ = ["qknorm_rope_scale", "qknorm_rope_scale_qkv", "prepare_backend", "RMSNormRoPEScale", "FusedQKV",
+           *_LAZY]
 
 
 def __getattr__(name):

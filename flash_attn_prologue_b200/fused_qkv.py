@@ -303,16 +303,20 @@ def fused_qkv_epilogue_op(
     scales: torch.Tensor,
     sin: torch.Tensor,
     cos: torch.Tensor,
+    eps: float = 1e-5,
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    # eps: a trailing optional argument beyond the reference's schema (which
+    # fixes 1e-5); callers of the reference's six-argument form are unaffected.
     head_dim, H = _check_prologue_params(x, weight, rmsnorm_weight, scales, sin, cos)
+    _check_eps(eps)
     outs = [_empty_bhnd(x, H, head_dim) for _ in range(3)]
     raws = [_empty_bhnd(x, H, head_dim) for _ in range(2)]
-    _launch(x, weight, head_dim, outs, raws, rmsnorm_weight, scales, sin, cos)
+    _launch(x, weight, head_dim, outs, raws, rmsnorm_weight, scales, sin, cos, eps)
     return outs[0], outs[1], outs[2], raws[0], raws[1]
 
 
 @fused_qkv_epilogue_op.register_fake
-def _fused_qkv_epilogue_fake(x, weight, rmsnorm_weight, scales, sin, cos):
+def _fused_qkv_epilogue_fake(x, weight, rmsnorm_weight, scales, sin, cos, eps=1e-5):
     head_dim = rmsnorm_weight.shape[-1]
     H = weight.shape[0] // (3 * head_dim)
     return tuple(torch.empty((x.shape[0], H, x.shape[1], head_dim), dtype=x.dtype, device=x.device)
@@ -346,15 +350,16 @@ def fused_qkv_epilogue_backward_op(
     x: torch.Tensor, weight: torch.Tensor, rmsnorm_weight: torch.Tensor, scales: torch.Tensor,
     sin: torch.Tensor, cos: torch.Tensor, q_proj: torch.Tensor, k_proj: torch.Tensor,
     grad_q: Optional[torch.Tensor], grad_k: Optional[torch.Tensor], grad_v: Optional[torch.Tensor],
+    eps: float = 1e-5,
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     """Backward of fused_qkv_epilogue from its saved BF16 projections (reference: fused_qkv.py:847-867)."""
     return _prologue_and_linear_backward(x, weight, rmsnorm_weight, scales, sin, cos, q_proj, k_proj,
-                                         grad_q, grad_k, grad_v)
+                                         grad_q, grad_k, grad_v, eps)
 
 
 @fused_qkv_epilogue_backward_op.register_fake
 def _fused_qkv_epilogue_backward_fake(x, weight, rmsnorm_weight, scales, sin, cos, q_proj, k_proj,
-                                      grad_q, grad_k, grad_v):
+                                      grad_q, grad_k, grad_v, eps=1e-5):
     D, H = q_proj.shape[-1], q_proj.shape[1]
     return (torch.empty_like(x), torch.empty_like(weight),
             torch.empty((2, 1, D), dtype=torch.float32, device=x.device),
@@ -362,9 +367,10 @@ def _fused_qkv_epilogue_backward_fake(x, weight, rmsnorm_weight, scales, sin, co
 
 
 def _fused_qkv_epilogue_setup(ctx, inputs, output):
-    x, weight, rmsnorm_weight, scales, sin, cos = inputs
+    x, weight, rmsnorm_weight, scales, sin, cos, eps = inputs
     _, _, _, q_proj, k_proj = output
     ctx.save_for_backward(x, weight, rmsnorm_weight, scales, sin, cos, q_proj, k_proj)
+    ctx.eps = eps
 
 
 def _fused_qkv_epilogue_backward(ctx, gq, gk, gv, g_qproj, g_kproj):
@@ -372,8 +378,8 @@ def _fused_qkv_epilogue_backward(ctx, gq, gk, gv, g_qproj, g_kproj):
     # reference (fused_qkv.py:847-867) gradients arriving on them are ignored.
     x, weight, rmsnorm_weight, scales, sin, cos, q_proj, k_proj = ctx.saved_tensors
     grad_x, grad_w, dw, ds = fused_qkv_epilogue_backward_op(
-        x, weight, rmsnorm_weight, scales, sin, cos, q_proj, k_proj, gq, gk, gv)
-    return grad_x, grad_w, dw, ds, None, None
+        x, weight, rmsnorm_weight, scales, sin, cos, q_proj, k_proj, gq, gk, gv, ctx.eps)
+    return grad_x, grad_w, dw, ds, None, None, None
 
 
 torch.library.register_autograd("flash_prologue::fused_qkv_epilogue", _fused_qkv_epilogue_backward,
@@ -395,20 +401,26 @@ def _check_prologue_params(x, weight, rmsnorm_weight, scales, sin, cos):
     return head_dim, H
 
 
+def _check_eps(eps):
+    if not (eps > 0.0) or eps == float("inf"):
+        raise ValueError("eps must be finite and positive")
+
+
 @torch.library.custom_op("flash_prologue::fused_qkv_epilogue_ckp", mutates_args=())
 def fused_qkv_epilogue_ckp_op(
     x: torch.Tensor, weight: torch.Tensor, rmsnorm_weight: torch.Tensor, scales: torch.Tensor,
-    sin: torch.Tensor, cos: torch.Tensor,
+    sin: torch.Tensor, cos: torch.Tensor, eps: float = 1e-5,
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """(q, k, v) of fused_qkv_epilogue without storing the pre-prologue projections."""
     head_dim, H = _check_prologue_params(x, weight, rmsnorm_weight, scales, sin, cos)
+    _check_eps(eps)
     outs = [_empty_bhnd(x, H, head_dim) for _ in range(3)]
-    _launch(x, weight, head_dim, outs, (None, None), rmsnorm_weight, scales, sin, cos)
+    _launch(x, weight, head_dim, outs, (None, None), rmsnorm_weight, scales, sin, cos, eps)
     return outs[0], outs[1], outs[2]
 
 
 @fused_qkv_epilogue_ckp_op.register_fake
-def _fused_qkv_epilogue_ckp_fake(x, weight, rmsnorm_weight, scales, sin, cos):
+def _fused_qkv_epilogue_ckp_fake(x, weight, rmsnorm_weight, scales, sin, cos, eps=1e-5):
     head_dim = rmsnorm_weight.shape[-1]
     H = weight.shape[0] // (3 * head_dim)
     return tuple(torch.empty((x.shape[0], H, x.shape[1], head_dim), dtype=x.dtype, device=x.device)
@@ -419,19 +431,19 @@ def _fused_qkv_epilogue_ckp_fake(x, weight, rmsnorm_weight, scales, sin, cos):
 def fused_qkv_epilogue_ckp_backward_op(
     x: torch.Tensor, weight: torch.Tensor, rmsnorm_weight: torch.Tensor, scales: torch.Tensor,
     sin: torch.Tensor, cos: torch.Tensor, grad_q: Optional[torch.Tensor],
-    grad_k: Optional[torch.Tensor], grad_v: Optional[torch.Tensor],
+    grad_k: Optional[torch.Tensor], grad_v: Optional[torch.Tensor], eps: float = 1e-5,
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     """Recomputes the BF16 projections (same kernel, bit-identical), then the fused backward."""
     head_dim, H = _check_prologue_params(x, weight, rmsnorm_weight, scales, sin, cos)
     proj = [_empty_bhnd(x, H, head_dim) for _ in range(3)]
     _launch(x, weight, head_dim, proj, (None, None))
     return _prologue_and_linear_backward(x, weight, rmsnorm_weight, scales, sin, cos, proj[0], proj[1],
-                                         grad_q, grad_k, grad_v)
+                                         grad_q, grad_k, grad_v, eps)
 
 
 @fused_qkv_epilogue_ckp_backward_op.register_fake
 def _fused_qkv_epilogue_ckp_backward_fake(x, weight, rmsnorm_weight, scales, sin, cos, grad_q, grad_k,
-                                          grad_v):
+                                          grad_v, eps=1e-5):
     D = rmsnorm_weight.shape[-1]
     H = weight.shape[0] // (3 * D)
     return (torch.empty_like(x), torch.empty_like(weight),
@@ -440,12 +452,13 @@ def _fused_qkv_epilogue_ckp_backward_fake(x, weight, rmsnorm_weight, scales, sin
 
 
 def _fused_qkv_epilogue_ckp_setup(ctx, inputs, output):
-    ctx.save_for_backward(*inputs)
+    ctx.save_for_backward(*inputs[:6])
+    ctx.eps = inputs[6]
 
 
 def _fused_qkv_epilogue_ckp_backward(ctx, gq, gk, gv):
-    grad_x, grad_w, dw, ds = fused_qkv_epilogue_ckp_backward_op(*ctx.saved_tensors, gq, gk, gv)
-    return grad_x, grad_w, dw, ds, None, None
+    grad_x, grad_w, dw, ds = fused_qkv_epilogue_ckp_backward_op(*ctx.saved_tensors, gq, gk, gv, ctx.eps)
+    return grad_x, grad_w, dw, ds, None, None, None
 
 
 torch.library.register_autograd("flash_prologue::fused_qkv_epilogue_ckp", _fused_qkv_epilogue_ckp_backward,

@@ -1,3 +1,4 @@
+from .FusedQKV import FusedQKV
 from .RMSNorm import RMSNormRoPEScale
 
-__all__ = ["RMSNormRoPEScale"]
+__all__ = ["FusedQKV", "RMSNormRoPEScale"]

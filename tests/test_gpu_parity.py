@@ -106,6 +106,17 @@ def test_packed_dims_dtypes(d, dtype):
     _compare_with_oracle(*[t.cuda() for t in args])
 
 
+@pytest.mark.parametrize("t", [1, 2, 63, 65, 129])
+@pytest.mark.parametrize("d", [32, 64, 128])
+@pytest.mark.parametrize("h", [1, 3])
+def test_tiny_odd_token_counts(t, d, h):
+    """Ragged tiles: token counts around the tile edges, one or three heads, fwd and bwd."""
+    args = _inputs((t, h, d), d, h, seed=t * 7 + d + h)
+    _compare_with_oracle(*[a.cuda() for a in args])
+    dense = _inputs((2, h, t, d), d, h, seed=t + d, dense_tables=(2, t, d // 2))
+    _compare_with_oracle(*[a.cuda() for a in dense])
+
+
 @pytest.mark.parametrize("d", [32, 64, 128, 256])
 @pytest.mark.parametrize("h", [1, 3, 8, 12, 32])
 def test_dense_heads(d, h):
