@@ -60,6 +60,7 @@ SIGNATURES = {
     "flash_prologue_qkv_bwd_dw": ([_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp, ctypes.c_int,
                                    _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64, _i64, _vp],
                                   ctypes.c_int),
+    "flash_prologue_copy_rows": ([_vp, _i64p, _vp, _i64p, _i64p, _i64, _vp], ctypes.c_int),
     "flash_prologue_set_path": ([ctypes.c_int], ctypes.c_int),
     "flash_prologue_set_gemm_variant": ([ctypes.c_int], ctypes.c_int),
     "flash_prologue_selftest_wait_timeout": ([ctypes.c_uint32, _vp], ctypes.c_int),
@@ -136,6 +137,47 @@ def check(status: int, what: str) -> None:
                   ERR_ALIGNMENT, ERR_WORKSPACE):
         raise ValueError(msg)
     raise PrologueError(msg)
+
+
+def copy_rows(dst: torch.Tensor, src: torch.Tensor) -> None:
+    """dst.copy_(src) on the device for same-shape, same-dtype tensors whose last
+    dimension is contiguous, by the library's strided row copy (dimensions that
+    are contiguous in both are merged into longer rows). Layouts the kernel
+    cannot take (more than three outer dimensions after merging, or rows and
+    strides that are not 16-byte multiples) use torch's copy."""
+    if dst.shape != src.shape or dst.dtype != src.dtype:
+        raise ValueError("copy_rows: shape and dtype must match")
+    if dst.device.type != "cuda" or src.device != dst.device:
+        raise ValueError("copy_rows: both tensors must be on the same CUDA device")
+    if dst.numel() == 0:
+        return
+    es = dst.element_size()
+    shape, ss, ds = list(dst.shape), list(src.stride()), list(dst.stride())
+    # drop extent-1 dims, then merge each dim into the next when contiguous in both
+    dims = [(n, a, b) for n, a, b in zip(shape, ss, ds) if n != 1] or [(1, 1, 1)]
+    if dims[-1][1] != 1 or dims[-1][2] != 1:
+        dst.copy_(src)
+        return
+    merged = [list(dims[-1])]
+    for n, a, b in reversed(dims[:-1]):
+        row = merged[0]
+        if a == row[0] * row[1] and b == row[0] * row[2]:
+            row[0] *= n
+        else:
+            merged.insert(0, [n, a, b])
+    row_bytes = merged[-1][0] * es
+    outer = merged[:-1]
+    if len(outer) > 3 or row_bytes % 16:
+        dst.copy_(src)
+        return
+    outer = [[1, 0, 0]] * (3 - len(outer)) + outer
+    status = load().flash_prologue_copy_rows(
+        ptr(src), strides3([o[1] * es for o in outer]), ptr(dst), strides3([o[2] * es for o in outer]),
+        strides3([o[0] for o in outer]), row_bytes, stream_of(dst.device))
+    if status == ERR_ALIGNMENT:
+        dst.copy_(src)
+        return
+    check(status, "flash_prologue_copy_rows")
 
 
 def strides4(t: torch.Tensor):

@@ -6,7 +6,8 @@ projection ``[B, N, 3*H*D]`` (Q heads | K heads | V heads), and the op returns
 ``(q, k, v)`` as contiguous ``[B, H, N, D]`` tensors -- Q and K through the
 prologue, V copied out. The reference runs its CuTe prologue op on contiguous
 copies of the Q and K slices (epilogue_kernel.py:222-243); here the kernels
-read the slices of ``qkv`` in place and write the contiguous outputs directly.
+read the slices of ``qkv`` in place and write the contiguous outputs directly
+(V by the library's row copy).
 Backward: the prologue backward kernel writes dq and dk straight into the Q/K
 slots of one ``[B, N, 3*H*D]`` gradient and dv is copied into its V slot
 (the exact gradient of the forward; the reference's backward is an eager
@@ -61,7 +62,8 @@ def qknorm_rope_scale_op(
     _check_common(q4, k4, rmsnorm_weight, scales, sin4, cos4, eps)
     q_out = torch.empty((B, H, N, D), dtype=qkv.dtype, device=qkv.device)
     k_out = torch.empty((B, H, N, D), dtype=qkv.dtype, device=qkv.device)
-    v_out = qkv5[:, :, 2].permute(0, 2, 1, 3).contiguous()
+    v_out = torch.empty((B, H, N, D), dtype=qkv.dtype, device=qkv.device)
+    _lib.copy_rows(v_out, qkv5[:, :, 2].permute(0, 2, 1, 3))
     if q4.numel() == 0:
         return q_out, k_out, v_out
     s4, sin_str = _table(sin4, B, N, D // 2)

@@ -488,7 +488,8 @@ def qknorm_rope_scale_qkv_backward_op(
     [B, H, N, D] views and grad_v that of the V slot as [B, N, H, D] (None =
     zero). grad_qkv has qkv's memory order; the backward kernel writes dq and
     dk into its Q and K slots through strided output views and grad_v is
-    copied into its V slot, so the caller needs no gather of slice gradients.
+    copied into its V slot by the library's row copy, so the caller needs no
+    gather of slice gradients.
     """
     if qkv.ndim != 5 or qkv.shape[2] != 3:
         raise ValueError("qkv must be [B,N,3,H,D]")
@@ -503,7 +504,7 @@ def qknorm_rope_scale_qkv_backward_op(
     if grad_v is None:
         grad_qkv[:, :, 2].zero_()
     else:
-        grad_qkv[:, :, 2].copy_(grad_v)
+        _lib.copy_rows(grad_qkv[:, :, 2], grad_v)
     return grad_qkv, grad_w, grad_s
 
 

@@ -250,6 +250,18 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_bwd_dw(const void* grad_q, const int64
                        void* stream);
 
 /*
+ * Strided row copy: dst[i0,i1,i2,:] = src[i0,i1,i2,:] for dims[0..2] outer
+ * indices (i2 fastest) and rows of row_bytes contiguous bytes, with byte
+ * strides src_strides / dst_strides. row_bytes, both base pointers and the
+ * strides of dimensions of extent > 1 must be multiples of 16. Moves the V
+ * slot of a fused QKV tensor or of its gradient (the reference does these
+ * with torch copies: epilogue_kernel.py:222-243, fused_epilogue.py:1399-1402).
+ */
+FLASH_PROLOGUE_API int flash_prologue_copy_rows(const void* src, const int64_t src_strides[3],
+                       void* dst, const int64_t dst_strides[3], const int64_t dims[3],
+                       int64_t row_bytes, void* stream);
+
+/*
  * Mainloop of flash_prologue_qkv_gemm_fwd (process-wide, not thread-safe; for
  * tests and tuning). 0 (default): CTA pairs -- 2-CTA clusters running
  * tcgen05.mma.cta_group::2 on 256 x 256 tiles, each CTA loading half of the
