@@ -3,7 +3,8 @@
 Same signature, validation order, messages and layouts as the reference
 frontend (flash_attn_prologue/functional.py:6-94). ``backend="cute"`` runs the
 sm_100a CUDA kernels of libflash_prologue.so through the
-``flash_prologue::qknorm_rope_scale_cute`` custom op; ``backend="native"`` is
+``flash_prologue::qknorm_rope_scale_cute`` custom op (plain eager calls take
+the op's own body directly, skipping the dispatch layers); ``backend="native"`` is
 the reference's own traceable PyTorch formulation, kept so callers that select
 it by name keep working. The two are separate choices made by the caller:
 the ``cute`` path never routes to ``native`` (empty inputs included).
@@ -103,8 +104,11 @@ def qknorm_rope_scale(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5, *, backe
             q4 = q4.contiguous()
         if k4.stride(-1) != 1 or any(n > 1 and st == 0 for n, st in zip(k4.shape, k4.stride())):
             k4 = k4.contiguous()
-        out_q, out_k = torch.ops.flash_prologue.qknorm_rope_scale_cute(
-            q4, k4, rmsnorm_weight, scales, s4, c4, eps)
+        if _plain_eager(q4, k4, rmsnorm_weight, scales, s4, c4):
+            out_q, out_k = _CuteEager.apply(q4, k4, rmsnorm_weight, scales, s4, c4, eps)
+        else:
+            out_q, out_k = torch.ops.flash_prologue.qknorm_rope_scale_cute(
+                q4, k4, rmsnorm_weight, scales, s4, c4, eps)
         if q.ndim == 3:
             # squeeze (a view in both directions), not out[0]: the backward of a
             # select would allocate zeros and scatter-copy every gradient.
@@ -119,6 +123,39 @@ def qknorm_rope_scale(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5, *, backe
 
     return ((transform(q, rmsnorm_weight[0]) * scale.exp()).to(q.dtype),
             transform(k, rmsnorm_weight[1]).to(k.dtype))
+
+
+def _plain_eager(*tensors) -> bool:
+    """True for an eager call on plain tensors: not compiled, traced, under a
+    functorch transform or on tensor subclasses (fake, meta wrappers, DTensor),
+    where the registered custom op must be what is recorded."""
+    if torch.compiler.is_compiling() or torch.jit.is_tracing():
+        return False
+    active = getattr(torch._C, "_are_functorch_transforms_active", None)
+    if active is not None and active():
+        return False
+    return all(type(t) is torch.Tensor for t in tensors)
+
+
+class _CuteEager(torch.autograd.Function):
+    """qknorm_rope_scale_cute for eager calls without the custom-op dispatch
+    layers (tens of microseconds on small problems): the same forward and
+    backward bodies (fused_epilogue.cute_forward / cute_backward), so the
+    same kernels and results as the registered op and its autograd."""
+
+    @staticmethod
+    def forward(ctx, q, k, rmsnorm_weight, scales, sin, cos, eps):
+        from .fused_epilogue import cute_forward
+        ctx.save_for_backward(q, k, rmsnorm_weight, scales, sin, cos)
+        ctx.eps = eps
+        return cute_forward(q, k, rmsnorm_weight, scales, sin, cos, eps)
+
+    @staticmethod
+    def backward(ctx, grad_q, grad_k):
+        from .fused_epilogue import cute_backward
+        q, k, rmsnorm_weight, scales, sin, cos = ctx.saved_tensors
+        dq, dk, dw, ds = cute_backward(q, k, rmsnorm_weight, scales, sin, cos, grad_q, grad_k, ctx.eps)
+        return dq, dk, dw, ds, None, None, None
 
 
 def _cute_tables(sin, cos, packed, B, N, half):

@@ -148,6 +148,11 @@ def qknorm_rope_scale_cute_op(
     cos: torch.Tensor,
     eps: float = 1e-5,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
+    return cute_forward(q, k, rmsnorm_weight, scales, sin, cos, eps)
+
+
+def cute_forward(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-5):
+    """The body of qknorm_rope_scale_cute (also called directly by the eager frontend)."""
     _check_raw(q, k)
     _check_common(q, k, rmsnorm_weight, scales, sin, cos, eps)
     B, H, N, D = (int(x) for x in q.shape)
@@ -217,6 +222,11 @@ def qknorm_rope_scale_cute_backward_op(
     grad_k_out: torch.Tensor,
     eps: float = 1e-5,
 ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    return cute_backward(q, k, rmsnorm_weight, scales, sin, cos, grad_q_out, grad_k_out, eps)
+
+
+def cute_backward(q, k, rmsnorm_weight, scales, sin, cos, grad_q_out, grad_k_out, eps=1e-5):
+    """The body of qknorm_rope_scale_cute_backward (also called by the eager frontend)."""
     _check_raw(q, k)
     _check_common(q, k, rmsnorm_weight, scales, sin, cos, eps)
     B, H, N, D = (int(x) for x in q.shape)

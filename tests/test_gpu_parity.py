@@ -330,3 +330,26 @@ def test_bounded_wait_timeout_is_reported_and_context_survives():
     ref = native_forward(*[t.detach().cpu() for t in args])
     _check_outputs(out, ref, torch.bfloat16, [t.detach().cpu() for t in args])
     assert _lib.device_error(reset=True) == 0
+
+
+def test_eager_path_equals_registered_op():
+    """Plain eager calls skip the custom-op dispatch; outputs and gradients are the op's bits."""
+    from flash_attn_prologue_b200.functional import _plain_eager
+    args = [t.cuda() for t in _inputs((300, 8, 64), 64, 8, seed=9)]
+    q, k, w, s, sin, cos = args
+    assert _plain_eager(q, k, w, s, sin, cos)
+    leaves = [t.detach().requires_grad_(i < 4) for i, t in enumerate(args)]
+    out = qknorm_rope_scale(*leaves, backend="cute")
+    g = [torch.randn_like(o) for o in out]
+    grads = torch.autograd.grad(out, leaves[:4], g)
+    q4, k4 = (t.detach().requires_grad_() for t in (q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None]))
+    w2, s2 = w.detach().requires_grad_(), s.detach().requires_grad_()
+    s4 = sin.permute(1, 0, 2)[None] if sin.ndim == 3 else sin[None, None]
+    c4 = cos.permute(1, 0, 2)[None] if cos.ndim == 3 else cos[None, None]
+    ref = torch.ops.flash_prologue.qknorm_rope_scale_cute(q4, k4, w2, s2, s4, c4, 1e-5)
+    rgrads = torch.autograd.grad(ref, (q4, k4, w2, s2), [t.permute(1, 0, 2)[None] for t in g])
+    assert torch.equal(out[0], ref[0].squeeze(0).permute(1, 0, 2))
+    assert torch.equal(out[1], ref[1].squeeze(0).permute(1, 0, 2))
+    assert torch.equal(grads[0], rgrads[0].squeeze(0).permute(1, 0, 2))
+    assert torch.equal(grads[1], rgrads[1].squeeze(0).permute(1, 0, 2))
+    assert torch.equal(grads[2], rgrads[2]) and torch.equal(grads[3], rgrads[3])
