@@ -192,5 +192,14 @@ def ptr(t: torch.Tensor):
     return ctypes.c_void_p(t.data_ptr())
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(device: torch.device):
+    """The current CUDA stream of ``device`` as a cudaStream_t (a direct query
+    of the raw handle where torch exposes one: a few microseconds less per call
+    than building a Stream object)."""
+    if _raw_stream is not None:
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        return ctypes.c_void_p(_raw_stream(index))
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
