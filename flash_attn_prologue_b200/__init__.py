@@ -24,9 +24,9 @@ _LAZY = {
     "fused_qkv": ("fused_qkv", "fused_qkv_op"),
     "fused_qkv_epilogue": ("fused_qkv", "fused_qkv_epilogue_op"),
     "fused_qkv_epilogue_ckp": ("fused_qkv", "fused_qkv_epilogue_ckp_op"),
-    "matmul_bwd_dx": ("fused_qkv", "matmul_bwd_dx"),
-    "matmul_bwd_dw": ("fused_qkv", "matmul_bwd_dw"),
-    "fused_qkv_backward": ("fused_qkv", "fused_qkv_backward"),
+    "matmul_bwd_dx": ("gemm_bwd", "matmul_bwd_dx"),
+    "matmul_bwd_dw": ("gemm_bwd", "matmul_bwd_dw"),
+    "fused_qkv_backward": ("gemm_bwd", "fused_qkv_backward"),
 }
 __all__ = ["qknorm_rope_scale", "qknorm_rope_scale_qkv", "prepare_backend", "RMSNormRoPEScale", "FusedQKV",
            *_LAZY]
@@ -36,10 +36,14 @@ def __getattr__(name):
     if name not in _LAZY:
         raise AttributeError(name)
     module, symbol = _LAZY[name]
-    loaded = import_module(f".{module}", __name__)
-    # Importing the submodule binds the package attribute of the same name to
-    # the module; restore every public alias that it provides.
+    import_module(f".{module}", __name__)
+    # Importing a submodule binds the package attribute of the same name to
+    # the module (``fused_qkv`` collides with the op alias), also for the
+    # submodules it imports in turn: restore every alias whose source module
+    # is loaded by now.
+    import sys
     for alias, (source, exported) in _LAZY.items():
-        if source == module:
-            globals()[alias] = getattr(loaded, exported)
+        mod = sys.modules.get(f"{__name__}.{source}")
+        if mod is not None:
+            globals()[alias] = getattr(mod, exported)
     return globals()[name]

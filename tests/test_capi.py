@@ -147,3 +147,19 @@ def test_compact_strides_match_reference_contract():
     assert _get_compact_strides((1, 16, 100, 64), (1, 64, 3072, 1)) == (1, 64, 1024, 1)
     assert _get_compact_strides((2, 4, 17, 32), (2176, 544, 32, 1)) == (2176, 544, 32, 1)
     assert _get_compact_strides((2, 4, 17, 32), (2176, 1, 128, 4)) == (2176, 1, 128, 4)
+
+
+def test_lazy_exports_resolve_to_ops_in_any_order():
+    """Package aliases under the reference's names stay the ops whichever submodule loads first
+    (``fused_qkv`` is also a submodule name); gemm_bwd keeps the reference's module path."""
+    import subprocess
+    import sys
+    code = (
+        "import flash_attn_prologue_b200 as f\n"
+        "a = f.matmul_bwd_dx\n"
+        "assert 'CustomOpDef' in repr(f.fused_qkv), repr(f.fused_qkv)\n"
+        "assert 'CustomOpDef' in repr(f.fused_qkv_epilogue)\n"
+        "from flash_attn_prologue_b200.gemm_bwd import fused_qkv_backward, matmul_bwd_dw\n"
+        "assert f.fused_qkv_backward is fused_qkv_backward\n"
+    )
+    subprocess.run([sys.executable, "-c", code], check=True, cwd=ROOT)
