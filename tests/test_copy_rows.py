@@ -64,3 +64,25 @@ def test_layouts_handed_to_torch():
     out = torch.empty_like(odd)
     _lib.copy_rows(out, odd)
     assert torch.equal(out, odd)
+
+
+@pytest.mark.gpu
+def test_random_layouts_match_torch_copy():
+    """Slices and permutations with the last dimension contiguous, merged or not."""
+    g = torch.Generator().manual_seed(0)
+    for trial in range(40):
+        shape = [int(torch.randint(1, 9, (1,), generator=g)) for _ in range(3)] + \
+                [int(torch.tensor([8, 16, 24, 32, 64])[torch.randint(0, 5, (1,), generator=g)])]
+        slot = int(torch.randint(0, 3, (1,), generator=g))
+        base = torch.randn(shape[0], shape[1], 3, shape[2], shape[3]).to(torch.bfloat16).cuda()
+        src = base[:, :, slot]                           # a slot of a fused buffer
+        perm = [0, 1, 2]
+        if trial % 2:
+            perm = [1, 0, 2] if trial % 4 == 1 else [2, 0, 1]
+        src = src.permute(*perm, 3)
+        dst = torch.empty(src.shape, dtype=src.dtype, device="cuda")
+        if trial % 3 == 0:                                # a strided destination as well
+            big = torch.zeros(*src.shape[:-1], 2 * src.shape[-1], dtype=src.dtype, device="cuda")
+            dst = big[..., : src.shape[-1]]
+        _lib.copy_rows(dst, src)
+        assert torch.equal(dst, src), (trial, shape, perm)
