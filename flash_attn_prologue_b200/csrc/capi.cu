@@ -196,7 +196,7 @@ int common_checks(const void* q, const int64_t* qs, const void* k, const int64_t
 // 0: automatic (bulk-copy pipeline when the layout allows it), 1: register path only.
 int g_path_mode = 0;
 
-constexpr int kFwdStages = 4;
+constexpr int kFwdStages = 3;
 constexpr int kBwdStages = 3;
 
 // A streamed input the bulk-copy path can read: 16-byte aligned, rows along
