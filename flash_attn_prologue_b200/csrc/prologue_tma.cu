@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
     const unsigned char* sin_s = st + 4 * kTmaTileBytes;
     const unsigned char* cos_s = sin_s + table_bytes;
     T* dtile = db + (int64_t)tc.b * sd.b + (int64_t)tc.i0 * sd_inner + (int64_t)tc.o0 * sd_outer + j0;
-#pragma unroll 1
+#pragma unroll
     for (int pass = 0; pass < S_::PASSES; ++pass) {
       const int r = pass * S_::ROWS_PER_PASS + slot;
       const int o_l = r >> a.p.log2_ti;
