@@ -491,7 +491,33 @@ def run_extras(device, steps=20):
     bwd["note"] = ("dx/dw = tcgen05 GEMM kernels reading the [B, H, N, D] gradients through TMA (no gather); "
                    "cublas_* = torch matmul on a dP already gathered to [T, 3HD], gather_dp = that gather")
     out["c5_projection_backward"] = bwd
-    del gq5, gk5, gv5, dp
+    # C5 training step: forward + backward to x, W, rmsnorm_weight and scales
+    # through the fused op, and through the reference's composition
+    # (cuBLAS F.linear, this prologue op, autograd's cuBLAS GEMMs for the linear).
+    xg = x.detach().requires_grad_()
+    wg = wq.detach().requires_grad_()
+    wr = w.detach().requires_grad_()
+    sr = s.detach().requires_grad_()
+    ups = (gq5, gk5, gv5)
+
+    def step_fused():
+        q_, k_, v_, _, _ = fap.fused_qkv_epilogue(xg, wg, wr, sr, sin, cos)
+        return torch.autograd.grad((q_, k_, v_), (xg, wg, wr, sr), ups)
+
+    def step_composed():
+        p = torch.nn.functional.linear(xg, wg).view(1, T, 3, H, D)
+        q_, k_ = qknorm_rope_scale(p[:, :, 0].transpose(1, 2), p[:, :, 1].transpose(1, 2), wr, sr, sin, cos,
+                                   backend="cute")
+        return torch.autograd.grad((q_, k_, p[:, :, 2].transpose(1, 2)), (xg, wg, wr, sr), ups)
+
+    step = {"fused_ms": round(_event_ms(step_fused, steps), 4),
+            "cublas_linear_and_prologue_ms": round(_event_ms(step_composed, steps), 4)}
+    step["speedup"] = round(step["cublas_linear_and_prologue_ms"] / step["fused_ms"], 3)
+    step["flop"] = 3 * flop
+    step["note"] = ("forward + backward to x, W, rmsnorm_weight, scales; 3 GEMMs of 2*M*N*K each; "
+                    "composed = F.linear (cuBLAS) + qknorm_rope_scale(cute) + autograd")
+    out["c5_training_step"] = step
+    del gq5, gk5, gv5, dp, xg, wg
     return out
 
 
