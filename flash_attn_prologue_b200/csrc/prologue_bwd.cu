@@ -3,7 +3,7 @@
 //
 // Per row (x = q or k, g = upstream gradient, e = exp(scales[h]) for Q, 1 for K),
 // the identities of the reference backward (flash_attn_prologue/fused_epilogue.py:1047-1126):
-//   r  = 1/sqrt(mean(x^2)+eps),  n = x*r
+//   r  = rsqrt(mean(x^2)+eps),  n = x*r
 //   g' = g*e
 //   dn_j = g'_j cos_j + g'_{j+D/2} sin_j,  dn_{j+D/2} = g'_{j+D/2} cos_j - g'_j sin_j
 //   d scales[h]   += sum_j g'_j * rot(n*w)_j  =  sum_j dn_j w_j n_j   (Q rows only;
@@ -11,6 +11,9 @@
 //                    product equals the one dx needs anyway)
 //   d w[t][j]     += dn_j * n_j
 //   dx_j = r * (dn_j w_j - n_j * sum_i(dn_i w_i n_i) / D)
+// evaluated with e folded into r (bwd_lane_reduce / bwd_lane_dx): with
+// d0 = R^T g and re = r e, dn = e d0, d w += d0 (x re), the row sum is
+// sum_i d0_i w_i (x_i re), and dx = re (d0 w) - x (r r sum / D).
 // The reference accumulates the two parameter gradients with float atomics
 // (fused_epilogue.py:1129-1207), whose order changes run to run. Here every
 // CTA owns fixed rows (persistent, round-robin items); its threads keep
@@ -114,9 +117,9 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
         for (int k = 0; k < Chunk<T>::kWords; ++k) { x1.w[k] = 0; x2.w[k] = 0; g1.w[k] = 0; g2.w[k] = 0; }
       }
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
-      float2 dnw1[kPairs], dnw2[kPairs];
+      float2 dnw1[kPairs], dnw2[kPairs];  // INV: dn w; otherwise u = d0 w
       float2 n1[kPairs], n2[kPairs];  // INV: the rebuilt normalised row
-      float r, dsum;
+      float r, re = 0.f, dsum;
       if constexpr (INV) {
         r = ok ? __ldg(rms + (b * a.H + h) * a.N + n) : 0.f;
         if (ok) {
@@ -128,9 +131,10 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
         dsum = row_sum<L>(bwd_lane_reduce_n(n1, n2, g1, g2, e, t == 0, w + j0, w + HALF + j0, sn, cs,
                                             acc1p, acc2p, dnw1, dnw2));
       } else {
-        r = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
-        dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, r, e, t == 0, w + j0, w + HALF + j0, sn,
-                                          cs, acc1p, acc2p, dnw1, dnw2));
+        r = inv_rms_bwd<D>(row_sum<L>(lane_sumsq2(x1, x2)), a.eps);
+        re = __fmul_rn(r, e);
+        dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, re, w + j0, w + HALF + j0, sn, cs, acc1p,
+                                          acc2p, dnw1, dnw2));
       }
       if (t == 0) {
         // d scales: the row's sum(dn w n), reduced over the warp's position slots.
@@ -144,7 +148,8 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
       if constexpr (INV)
         bwd_lane_dx_n<T>(n1, n2, r, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
       else
-        bwd_lane_dx(x1, x2, r, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
+        bwd_lane_dx(x1, x2, re, __fmul_rn(r, __fmul_rn(r, dsum * (1.0f / (float)D))), dnw1, dnw2,
+                    out1, out2);
       T* dp = db + b * sd.b + (int64_t)h * sd.h + n * sd.n + j0;
       store_stream<T, VEC>(dp, out1);
       store_stream<T, VEC>(dp + HALF, out2);

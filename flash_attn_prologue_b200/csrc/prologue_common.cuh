@@ -227,6 +227,17 @@ __device__ __forceinline__ float inv_rms(float sumsq, float eps) {
   return __frcp_rn(__fsqrt_rn(__fadd_rn(mean, eps)));
 }
 
+// The backward's recomputed r: the hardware reciprocal square root
+// (rsqrt.approx.f32, relative error below 2^-22), as the reference's CuTe
+// backward recomputes its per-row rstd (cute.math.rsqrt,
+// flash_attn_prologue/fused_epilogue.py:1055-1056). Gradients carry a
+// tolerance, so the backward does not pay for the IEEE-rounded sequence.
+template <int D>
+__device__ __forceinline__ float inv_rms_bwd(float sumsq, float eps) {
+  static_assert((D & (D - 1)) == 0, "head dim must be a power of two");
+  return rsqrtf(__fadd_rn(__fmul_rn(sumsq, 1.0f / (float)D), eps));
+}
+
 // ---------------------------------------------------------------------------
 // Per-row arithmetic shared by the register-path and the bulk-copy kernels (so
 // both give bit-identical results). A lane holds the chunk pair
@@ -287,6 +298,21 @@ __device__ __forceinline__ float lane_sumsq(const Chunk<T>& x1, const Chunk<T>& 
   return __fadd_rn(acc.x, acc.y);
 }
 
+// lane_sumsq with the two halves summed in independent chains (backward only:
+// its r carries no bit-parity requirement, and the shorter chain hides latency).
+template <typename T>
+__device__ __forceinline__ float lane_sumsq2(const Chunk<T>& x1, const Chunk<T>& x2) {
+  float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int p = 0; p < kPairs; ++p) {
+    const float2 u = chunk_get2(x1, p), v = chunk_get2(x2, p);
+    a = (sizeof(T) == 2) ? __ffma2_rn(u, u, a) : __fadd2_rn(a, __fmul2_rn(u, u));
+    b = (sizeof(T) == 2) ? __ffma2_rn(v, v, b) : __fadd2_rn(b, __fmul2_rn(v, v));
+  }
+  const float2 s = __fadd2_rn(a, b);
+  return __fadd_rn(s.x, s.y);
+}
+
 // Forward outputs of one lane: normed = (x * r) * w, rotated, times e for Q.
 // Every product and sum rounds separately, as in the eager formulation
 // (a - b is computed as a + (-b), which rounds identically).
@@ -314,54 +340,57 @@ __device__ __forceinline__ void fwd_lane(const Chunk<T>& x1, const Chunk<T>& x2,
   chunk_set2(out2, o2);
 }
 
-// Backward, reduction part of one lane. With g' = g * e (e = exp(scale) for Q,
-// 1 for K) and dn = R^T g' (inverse rotation), it accumulates the d w partials
-// acc += dn * n (n = x * r), keeps dnw = dn * w for the dx part, and returns
-// the lane partial of sum_j dn_j w_j n_j. That sum is also the row's
-// contribution to d scale: <R^T g', n w> = <g', R(n w)> = sum_j dq_out_j q_out_j.
+// Backward, reduction part of one lane. With d0 = R^T g (the inverse rotation
+// of the upstream gradient, without the Q scale e) and re = r * e (r for K):
+// dy = e d0 is the gradient of the normed row n w and dn = dy w = e u with
+// u = d0 w, so
+//   d w partial:  acc += d0 * (x re)                        (= dy n)
+//   returned:     lane partial of sum_j u_j (x_j re)        (= <dn, n>)
+// and u is kept for the dx part. The returned sum is also the row's
+// contribution to d scale: <dn, n> = <R^T g', n w> = <g', R(n w)> =
+// sum_j dq_out_j q_out_j. Two independent partial sums (first / second half)
+// shorten the dependency chain.
 template <typename T>
 __device__ __forceinline__ float bwd_lane_reduce(const Chunk<T>& x1, const Chunk<T>& x2,
-                                                 const Chunk<T>& g1, const Chunk<T>& g2, float r,
-                                                 float e, bool scale, const float* wa,
-                                                 const float* wb, const float (&sn)[kChunk],
-                                                 const float (&cs)[kChunk],
+                                                 const Chunk<T>& g1, const Chunk<T>& g2, float re,
+                                                 const float* wa, const float* wb,
+                                                 const float (&sn)[kChunk], const float (&cs)[kChunk],
                                                  float2 (&acc1)[kPairs], float2 (&acc2)[kPairs],
-                                                 float2 (&dnw1)[kPairs], float2 (&dnw2)[kPairs]) {
-  const float2 r2 = splat2(r), e2 = splat2(e);
-  float2 dsum = make_float2(0.f, 0.f);
+                                                 float2 (&u1)[kPairs], float2 (&u2)[kPairs]) {
+  const float2 re2 = splat2(re);
+  float2 ds1 = make_float2(0.f, 0.f), ds2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int p = 0; p < kPairs; ++p) {
     const float2 c2 = make_float2(cs[2 * p], cs[2 * p + 1]);
     const float2 s2 = make_float2(sn[2 * p], sn[2 * p + 1]);
-    float2 ga = chunk_get2(g1, p), gb = chunk_get2(g2, p);
-    if (scale) { ga = __fmul2_rn(ga, e2); gb = __fmul2_rn(gb, e2); }
+    const float2 ga = chunk_get2(g1, p), gb = chunk_get2(g2, p);
     const float2 d1 = __ffma2_rn(ga, c2, __fmul2_rn(gb, s2));
     const float2 d2 = __ffma2_rn(gb, c2, neg2(__fmul2_rn(ga, s2)));
-    const float2 n1 = __fmul2_rn(chunk_get2(x1, p), r2);
-    const float2 n2 = __fmul2_rn(chunk_get2(x2, p), r2);
+    const float2 n1 = __fmul2_rn(chunk_get2(x1, p), re2);
+    const float2 n2 = __fmul2_rn(chunk_get2(x2, p), re2);
     acc1[p] = __ffma2_rn(d1, n1, acc1[p]);
     acc2[p] = __ffma2_rn(d2, n2, acc2[p]);
-    dnw1[p] = __fmul2_rn(d1, ld_pair(wa, p));
-    dnw2[p] = __fmul2_rn(d2, ld_pair(wb, p));
-    dsum = __ffma2_rn(dnw1[p], n1, dsum);
-    dsum = __ffma2_rn(dnw2[p], n2, dsum);
+    u1[p] = __fmul2_rn(d1, ld_pair(wa, p));
+    u2[p] = __fmul2_rn(d2, ld_pair(wb, p));
+    ds1 = __ffma2_rn(u1[p], n1, ds1);
+    ds2 = __ffma2_rn(u2[p], n2, ds2);
   }
-  return __fadd_rn(dsum.x, dsum.y);
+  const float2 ds = __fadd2_rn(ds1, ds2);
+  return __fadd_rn(ds.x, ds.y);
 }
 
-// Backward, dx of one lane: dx = r * (dn w - n * m), m = sum(dn w n) / D.
+// Backward, dx of one lane: dx = r (dn - n m) with dn = e u, n = x r and
+// m = <dn, n> / D, evaluated as re * u - x * kx with kx = r * r * m.
 template <typename T>
-__device__ __forceinline__ void bwd_lane_dx(const Chunk<T>& x1, const Chunk<T>& x2, float r, float m,
-                                            const float2 (&dnw1)[kPairs], const float2 (&dnw2)[kPairs],
+__device__ __forceinline__ void bwd_lane_dx(const Chunk<T>& x1, const Chunk<T>& x2, float re, float kx,
+                                            const float2 (&u1)[kPairs], const float2 (&u2)[kPairs],
                                             Chunk<T>& out1, Chunk<T>& out2) {
-  const float2 r2 = splat2(r), nm2 = splat2(-m);
+  const float2 re2 = splat2(re), nk2 = splat2(-kx);
   float2 o1[kPairs], o2[kPairs];
 #pragma unroll
   for (int p = 0; p < kPairs; ++p) {
-    const float2 n1 = __fmul2_rn(chunk_get2(x1, p), r2);
-    const float2 n2 = __fmul2_rn(chunk_get2(x2, p), r2);
-    o1[p] = __fmul2_rn(r2, __ffma2_rn(n1, nm2, dnw1[p]));
-    o2[p] = __fmul2_rn(r2, __ffma2_rn(n2, nm2, dnw2[p]));
+    o1[p] = __ffma2_rn(chunk_get2(x1, p), nk2, __fmul2_rn(re2, u1[p]));
+    o2[p] = __ffma2_rn(chunk_get2(x2, p), nk2, __fmul2_rn(re2, u2[p]));
   }
   chunk_set2(out1, o1);
   chunk_set2(out2, o2);

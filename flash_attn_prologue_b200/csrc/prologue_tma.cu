@@ -381,9 +381,9 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       }
       const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
-      float2 dnw1[kPairs], dnw2[kPairs];
+      float2 dnw1[kPairs], dnw2[kPairs];  // INV: dn w; otherwise u = d0 w
       float2 n1[kPairs], n2[kPairs];  // INV: the rebuilt normalised row
-      float rr, dsum;
+      float rr, re = 0.f, dsum;
       if constexpr (INV) {
         rr = pass == 0 ? rv0 : rv1;
         if (ok) {
@@ -395,9 +395,10 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
         dsum = row_sum<L>(bwd_lane_reduce_n(n1, n2, g1, g2, e, t == 0, wa, wb, sn, cs, acc1p, acc2p,
                                             dnw1, dnw2));
       } else {
-        rr = inv_rms<D>(row_sum<L>(lane_sumsq(x1, x2)), a.eps);
-        dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, rr, e, t == 0, wa, wb, sn, cs, acc1p,
-                                          acc2p, dnw1, dnw2));
+        rr = inv_rms_bwd<D>(row_sum<L>(lane_sumsq2(x1, x2)), a.eps);
+        re = __fmul_rn(rr, e);
+        dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, re, wa, wb, sn, cs, acc1p, acc2p, dnw1,
+                                          dnw2));
       }
       if (t == 0) {
         float v = dsum;
@@ -410,7 +411,8 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       if constexpr (INV)
         bwd_lane_dx_n<T>(n1, n2, rr, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
       else
-        bwd_lane_dx(x1, x2, rr, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
+        bwd_lane_dx(x1, x2, re, __fmul_rn(rr, __fmul_rn(rr, dsum * (1.0f / (float)D))), dnw1, dnw2,
+                    out1, out2);
       T* dp = dtile + (int64_t)i_l * sd_inner + (int64_t)o_l * sd_outer;
       store_stream<T, true>(dp, out1);
       store_stream<T, true>(dp + HALF, out2);
