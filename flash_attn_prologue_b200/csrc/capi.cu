@@ -7,6 +7,7 @@
 
 #include "../../include/flash_prologue.h"
 #include "prologue_host.h"
+#include "tensor_map.h"
 
 namespace flash_prologue {
 
@@ -199,19 +200,31 @@ int g_path_mode = 0;
 constexpr int kFwdStages = 3;
 constexpr int kBwdStages = 3;
 
-// A streamed input the bulk-copy path can read: 16-byte aligned, rows along
-// the inner dim contiguous (stride D), b and outer strides 16-byte multiples.
-bool tma_tensor_ok(const void* p, const int64_t s[4], int64_t D, size_t es, bool heads_inner,
-                   TmaTensor* out) {
+// A streamed input the TMA path can read: 16-byte aligned, rows along the
+// inner dim contiguous (stride D), positive b and outer strides that are
+// 16-byte multiples, and a tensor map the driver accepts (the 5-D half-row
+// view of TmaTensor, prologue_host.h). Dims of extent 1 get a placeholder
+// stride (no address depends on it).
+bool tma_tensor_ok(const void* p, const int64_t s[4], int64_t B, int64_t D, int dtype,
+                   bool heads_inner, const TmaPlan& plan, TmaTensor* out) {
+  const int64_t es = (int64_t)elem_size(dtype);
   if (!aligned16(p) || s[3] != 1) return false;
   const int64_t s_inner = heads_inner ? s[1] : s[2];
   const int64_t s_outer = heads_inner ? s[2] : s[1];
   if (s_inner != D) return false;
-  if (((s[0] * (int64_t)es) & 15) != 0 || ((s_outer * (int64_t)es) & 15) != 0) return false;
-  out->base = static_cast<const char*>(p);
-  out->sb = s[0];
-  out->s_outer = s_outer;
-  return true;
+  const int64_t row = D * es;
+  int64_t sb = s[0] * es, so = s_outer * es;
+  if (B == 1) sb = row;
+  if (plan.outer_ext == 1) so = row;
+  if (sb <= 0 || so <= 0 || (sb & 15) != 0 || (so & 15) != 0) return false;
+  const uint64_t dims[5] = {(uint64_t)(D / 2), (uint64_t)plan.inner_ext, (uint64_t)plan.outer_ext, 2,
+                            (uint64_t)B};
+  const uint64_t strides[4] = {(uint64_t)row, (uint64_t)so, (uint64_t)(row / 2), (uint64_t)sb};
+  const uint32_t box[5] = {(uint32_t)(D / 2), (uint32_t)plan.ti, (uint32_t)plan.to, 2, 1};
+  const CUtensorMapDataType type = dtype == 0   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                   : dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  return encode_tensor_map(&out->map, type, 5, p, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 // sin/cos tables the bulk-copy path can read: rows of D/2 contiguous floats.
@@ -299,8 +312,9 @@ int fwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (g_path_mode == 0 && vec) {
     TmaFwdArgs t{};
-    if (tma_tensor_ok(q, q_strides, D, es, heads_inner, &t.in[0]) &&
-        tma_tensor_ok(k, k_strides, D, es, heads_inner, &t.in[1]) &&
+    t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kFwdStages);
+    if (tma_tensor_ok(q, q_strides, B, D, dtype, heads_inner, t.p, &t.in[0]) &&
+        tma_tensor_ok(k, k_strides, B, D, dtype, heads_inner, t.p, &t.in[1]) &&
         tma_table_ok(sin, sin_strides, N, D) && tma_table_ok(cos, cos_strides, N, D)) {
       t.out[0] = q_out; t.out[1] = k_out;
       t.so[0] = rows(q_out_strides); t.so[1] = rows(k_out_strides);
@@ -308,7 +322,6 @@ int fwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
       t.sin_b = sin_strides[0]; t.cos_b = cos_strides[0];
       t.rms[0] = rms_q; t.rms[1] = rms_k;
       t.B = B; t.N = N; t.H = (int)H; t.eps = eps;
-      t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kFwdStages);
       cudaError_t err = launch_fwd_tma(t, dtype, (int)D, s);
       return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
     }
@@ -442,12 +455,12 @@ int bwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
   const bool heads_inner = heads_inner_layout(q_strides, H, N);
   if (g_path_mode == 0 && vec) {
     TmaBwdArgs t{};
-    if (tma_tensor_ok(q, q_strides, D, es, heads_inner, &t.in[0]) &&
-        tma_tensor_ok(grad_q_out, gq_strides, D, es, heads_inner, &t.in[1]) &&
-        tma_tensor_ok(k, k_strides, D, es, heads_inner, &t.in[2]) &&
-        tma_tensor_ok(grad_k_out, gk_strides, D, es, heads_inner, &t.in[3]) &&
+    t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kBwdStages);
+    if (tma_tensor_ok(q, q_strides, B, D, dtype, heads_inner, t.p, &t.in[0]) &&
+        tma_tensor_ok(grad_q_out, gq_strides, B, D, dtype, heads_inner, t.p, &t.in[1]) &&
+        tma_tensor_ok(k, k_strides, B, D, dtype, heads_inner, t.p, &t.in[2]) &&
+        tma_tensor_ok(grad_k_out, gk_strides, B, D, dtype, heads_inner, t.p, &t.in[3]) &&
         tma_table_ok(sin, sin_strides, N, D) && tma_table_ok(cos, cos_strides, N, D)) {
-      t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kBwdStages);
       const int64_t tgrid = tma_grid(true, t.p, (int)H, (int)D, dtype, inv);
       if (tgrid <= 0) return FLASH_PROLOGUE_ERR_CUDA;
       const size_t tneed = (size_t)tgrid * (size_t)(2 * D + H) * sizeof(float);

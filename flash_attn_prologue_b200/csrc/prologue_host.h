@@ -1,6 +1,7 @@
 // Host-side structures shared by the C-ABI layer and the kernel launchers.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -52,6 +53,12 @@ constexpr int kTmaConsumerWarps = 8;                       // 0-3: Q rows, 4-7: 
 constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kTmaTileBytes = 8192;                        // per streamed tensor per stage
 
+// Bytes of one pipeline stage: `nt` streamed tiles, then the sin and cos rows,
+// rounded up so that every stage (each TMA destination) stays 128-byte aligned.
+__host__ __device__ constexpr int tma_stage_bytes(int nt, int table_bytes) {
+  return (nt * kTmaTileBytes + 2 * table_bytes + 127) & ~127;
+}
+
 // The backward kernel runs the 8 consumer warps (warpgroups 0-1) beside a
 // whole producer warpgroup (warp 8 issues the copies; warps 9-11 leave once
 // the group has given its registers back). It is launched at
@@ -77,10 +84,14 @@ struct TmaPlan {
   Radix4 radix;                  // digits (inner block, outer block, b); set at launch
 };
 
-// One streamed input: rows along the inner dim are contiguous (stride D).
-struct TmaTensor {
-  const char* base;
-  int64_t sb, s_outer;  // element strides of b and of the outer row dim
+// One streamed input, read by tiled TMA loads. The tensor map views it as 5-D
+// {D/2, inner, outer, 2, B}: a half row, the inner and outer row dims, the two
+// halves (stride D/2) and the batch. A box {D/2, ti, to, 2, 1} therefore lands
+// in shared memory as [half][outer][inner][D/2] -- the tile's first halves,
+// then its second halves -- so the lanes of a quarter warp, which read the
+// same half of consecutive rows, read 128 contiguous bytes (no bank conflicts).
+struct alignas(64) TmaTensor {
+  CUtensorMap map;
 };
 
 struct TmaFwdArgs {

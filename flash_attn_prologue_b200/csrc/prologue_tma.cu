@@ -6,14 +6,15 @@
 // of rows of one batch b: `ti` consecutive rows along the "inner" row dim
 // (heads for packed [T,H,D] views, positions for dense [B,H,N,D]), whose rows
 // are contiguous in memory (inner stride == D), times `to` indices of the outer
-// row dim. For every tile the producer warp issues one cp.async.bulk per outer
-// index and input tensor (2 KB - 8 KB each, merged into one when the whole tile
-// is contiguous) plus one per sin/cos table block, completing on the stage's
-// full barrier. Consumer warps 0-3 process the Q rows of the stage, warps 4-7
-// the K rows: each lane owns one 16-element chunk pair of a row (the split-half
-// RoPE partner of each element is in the same lane), reads it from shared
-// memory, and writes its results straight to global memory with 16-byte
-// streaming stores. Stages are recycled through the empty barriers.
+// row dim. For every tile the producer warp issues one tiled TMA load per input
+// tensor (a 5-D box that stores the tile's first half rows, then its second
+// half rows: TmaTensor in prologue_host.h) plus one bulk copy per sin/cos table
+// block, completing on the stage's full barrier. Consumer warps 0-3 process the
+// Q rows of the stage, warps 4-7 the K rows: each lane owns one 16-element
+// chunk pair of a row (the split-half RoPE partner of each element is in the
+// same lane), reads it from shared memory without bank conflicts, and writes
+// its results straight to global memory with 16-byte streaming stores. Stages
+// are recycled through the empty barriers.
 //
 // The arithmetic per row is the one of the register-path kernels
 // (prologue_fwd.cu / prologue_bwd.cu), in the same order, so both paths give
@@ -36,6 +37,8 @@ struct TmaShape {
   static constexpr int L = D / 16;                               // lanes per row
   static constexpr int LOG2_L = (L == 2) ? 1 : (L == 4) ? 2 : (L == 8) ? 3 : 4;
   static constexpr int HALF = D / 2;
+  static constexpr int HALF_BYTES = HALF * ES;                   // a half row in shared memory
+  static constexpr int HALF_TILE = ROWS * HALF_BYTES;            // first halves, then second halves
   static constexpr int GROUP_THREADS = kTmaConsumerWarps / 2 * 32;  // per tensor
   static constexpr int ROWS_PER_PASS = GROUP_THREADS / L;
   static constexpr int PASSES = ROWS / ROWS_PER_PASS;
@@ -59,56 +62,24 @@ __device__ __forceinline__ TileCoords tile_coords(const TmaPlan& p, const Cursor
   return tc;
 }
 
-// Issues the bulk copies of one stage: `nt` streamed tensors then sin and cos.
-// Called by the whole producer warp; lane 0 has already armed the barrier.
-template <int D, int ES>
-__device__ __forceinline__ void issue_stage(const TmaPlan& p, const TmaTensor* in, int nt,
-                                            const float* sin, const float* cos, int64_t sin_b,
-                                            int64_t cos_b, const TileCoords& tc, unsigned char* st,
-                                            int table_bytes, uint64_t* bar, int lane,
-                                            uint64_t pol_stream, uint64_t pol_table) {
-  constexpr int ROW_BYTES = D * ES;
-  const uint32_t run = (uint32_t)tc.vi * ROW_BYTES;  // bytes of one inner run
-  int copies_per_tensor = tc.vo;
-  bool merged[4];
-  for (int t = 0; t < nt; ++t) {
-    merged[t] = tc.vi == p.ti && in[t].s_outer == (int64_t)p.ti * D;
+// Issues the copies of one stage: lane t < nt loads streamed tensor t's tile
+// with one tiled TMA load (rows outside the tensor read as zeros), lanes nt and
+// nt + 1 copy the tile's sin and cos rows. Lane 0 has already armed the barrier.
+template <int D>
+__device__ __forceinline__ void issue_stage(const TmaTensor* in, int nt, const float* sin,
+                                            const float* cos, int64_t sin_b, int64_t cos_b,
+                                            int64_t n_first, int np, const TileCoords& tc,
+                                            unsigned char* st, int table_bytes, uint64_t* bar,
+                                            int lane, uint64_t pol_stream, uint64_t pol_table) {
+  if (lane < nt) {
+    tma_load_5d_hint(st + lane * kTmaTileBytes, &in[lane].map, 0, tc.i0, tc.o0, 0, tc.b, bar,
+                     pol_stream);
+  } else if (lane < nt + 2) {
+    const bool is_cos = lane == nt + 1;
+    const float* src = (is_cos ? cos : sin) + (int64_t)tc.b * (is_cos ? cos_b : sin_b) + n_first * (D / 2);
+    bulk_g2s(st + nt * kTmaTileBytes + (is_cos ? table_bytes : 0), src, (uint32_t)np * (D / 2) * 4,
+             bar, pol_table);
   }
-  // Copy list: per tensor (merged: one copy of vo runs) then two table copies.
-  int n_copies = 2;
-  for (int t = 0; t < nt; ++t) n_copies += merged[t] ? 1 : copies_per_tensor;
-  const int64_t n_first = p.heads_inner ? (int64_t)tc.o0 : (int64_t)tc.i0;
-  const int np = p.heads_inner ? tc.vo : tc.vi;
-  for (int j = lane; j < n_copies; j += 32) {
-    int jj = j;
-    int t = 0;
-    for (; t < nt; ++t) {
-      const int cnt = merged[t] ? 1 : copies_per_tensor;
-      if (jj < cnt) break;
-      jj -= cnt;
-    }
-    if (t < nt) {
-      const TmaTensor& x = in[t];
-      const int64_t o = (int64_t)tc.o0 + jj;
-      const char* src = x.base + ((int64_t)tc.b * x.sb + o * x.s_outer + (int64_t)tc.i0 * D) * ES;
-      unsigned char* dst = st + t * kTmaTileBytes + jj * p.ti * ROW_BYTES;
-      const uint32_t bytes = merged[t] ? run * (uint32_t)tc.vo : run;
-      bulk_g2s(dst, src, bytes, bar, pol_stream);
-    } else {
-      const bool is_cos = jj == 1;
-      const float* tab = is_cos ? cos : sin;
-      const int64_t tb = is_cos ? cos_b : sin_b;
-      const float* src = tab + (int64_t)tc.b * tb + n_first * (D / 2);
-      unsigned char* dst = st + nt * kTmaTileBytes + (is_cos ? table_bytes : 0);
-      bulk_g2s(dst, src, (uint32_t)np * (D / 2) * 4, bar, pol_table);
-    }
-  }
-}
-
-template <int D, int ES>
-__device__ __forceinline__ uint32_t stage_tx_bytes(const TmaPlan& p, int nt, const TileCoords& tc) {
-  const int np = p.heads_inner ? tc.vo : tc.vi;
-  return (uint32_t)nt * tc.vo * tc.vi * D * ES + 2u * np * (D / 2) * 4;
 }
 
 // 8 values of the activation dtype from shared memory (16 or 32 bytes).
@@ -142,7 +113,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   extern __shared__ __align__(128) unsigned char smem[];
   const int S = a.p.stages;
   const int table_bytes = a.p.P * HALF * 4;
-  const int stage_bytes = 2 * kTmaTileBytes + 2 * table_bytes;
+  const int stage_bytes = tma_stage_bytes(2, table_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
   uint64_t* empty = full + S;
   float* w_s = reinterpret_cast<float*>(empty + S);
@@ -171,10 +142,12 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
       const TileCoords tc = tile_coords(a.p, cur);
       unsigned char* st = smem + s * stage_bytes;
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], stage_tx_bytes<D, sizeof(T)>(a.p, 2, tc));
+      const int64_t n_first = a.p.heads_inner ? (int64_t)tc.o0 : (int64_t)tc.i0;
+      const int np = a.p.heads_inner ? tc.vo : tc.vi;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], 2 * kTmaTileBytes + 2 * np * HALF * 4);
       __syncwarp();
-      issue_stage<D, sizeof(T)>(a.p, a.in, 2, a.sin, a.cos, a.sin_b, a.cos_b, tc, st, table_bytes,
-                                &full[s], lane, pol_stream, pol_table);
+      issue_stage<D>(a.in, 2, a.sin, a.cos, a.sin_b, a.cos_b, n_first, np, tc, st, table_bytes,
+                     &full[s], lane, pol_stream, pol_table);
     }
     return;
   }
@@ -207,10 +180,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       const int o_l = r >> a.p.log2_ti;
       const int i_l = r & (a.p.ti - 1);
       const bool ok = o_l < tc.vo && i_l < tc.vi;
-      const unsigned char* row = tile_x + r * S_::ROW_BYTES;
+      const unsigned char* row = tile_x + r * S_::HALF_BYTES + j0 * sizeof(T);
       Chunk<T> x1, x2;
-      lds_chunk(x1, row + j0 * sizeof(T));
-      lds_chunk(x2, row + (HALF + j0) * sizeof(T));
+      lds_chunk(x1, row);
+      lds_chunk(x2, row + S_::HALF_TILE);
       const float ss = row_sum<L>(lane_sumsq(x1, x2));
       if (!ok) continue;
       const float rr = inv_rms<D>(ss, a.eps);
@@ -257,7 +230,7 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
   extern __shared__ __align__(128) unsigned char smem[];
   const int S = a.p.stages;
   const int table_bytes = a.p.P * HALF * 4;
-  const int stage_bytes = 4 * kTmaTileBytes + 2 * table_bytes;
+  const int stage_bytes = tma_stage_bytes(4, table_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
   uint64_t* empty = full + S;
   float* w_s = reinterpret_cast<float*>(empty + S);   // [2 * D]
@@ -297,10 +270,12 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
       const TileCoords tc = tile_coords(a.p, cur);
       unsigned char* st = smem + s * stage_bytes;
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], stage_tx_bytes<D, sizeof(T)>(a.p, 4, tc));
+      const int64_t n_first = a.p.heads_inner ? (int64_t)tc.o0 : (int64_t)tc.i0;
+      const int np = a.p.heads_inner ? tc.vo : tc.vi;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], 4 * kTmaTileBytes + 2 * np * HALF * 4);
       __syncwarp();
-      issue_stage<D, sizeof(T)>(a.p, a.in, 4, a.sin, a.cos, a.sin_b, a.cos_b, tc, st, table_bytes,
-                                &full[s], lane, pol_stream, pol_table);
+      issue_stage<D>(a.in, 4, a.sin, a.cos, a.sin_b, a.cos_b, n_first, np, tc, st, table_bytes,
+                     &full[s], lane, pol_stream, pol_table);
     }
     return;
   }
@@ -364,12 +339,12 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       Chunk<T> x1, x2, g1, g2;
       float sn[kChunk], cs[kChunk];
       if (ok) {
-        const unsigned char* xr = tile_x + r * S_::ROW_BYTES;
-        const unsigned char* gr = tile_g + r * S_::ROW_BYTES;
-        lds_chunk(x1, xr + j0 * sizeof(T));
-        lds_chunk(x2, xr + (HALF + j0) * sizeof(T));
-        lds_chunk(g1, gr + j0 * sizeof(T));
-        lds_chunk(g2, gr + (HALF + j0) * sizeof(T));
+        const unsigned char* xr = tile_x + r * S_::HALF_BYTES + j0 * sizeof(T);
+        const unsigned char* gr = tile_g + r * S_::HALF_BYTES + j0 * sizeof(T);
+        lds_chunk(x1, xr);
+        lds_chunk(x2, xr + S_::HALF_TILE);
+        lds_chunk(g1, gr);
+        lds_chunk(g2, gr + S_::HALF_TILE);
         const int p_l = a.p.heads_inner ? o_l : i_l;
         lds_f8(sn, sin_s + (p_l * HALF + j0) * 4);
         lds_f8(cs, cos_s + (p_l * HALF + j0) * 4);
@@ -499,8 +474,7 @@ cudaError_t read_device_error(int* value, bool reset) {
 }
 
 size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv) {
-  const size_t table = (size_t)p.P * (D / 2) * 4;
-  const size_t stage = (size_t)n_tensors * kTmaTileBytes + 2 * table;
+  const size_t stage = (size_t)tma_stage_bytes(n_tensors, p.P * (D / 2) * 4);
   size_t extra = (size_t)2 * p.stages * sizeof(uint64_t) + (size_t)(2 * D + H) * 4;
   if (n_tensors == 4) extra += (size_t)(4 * H + 8 * D) * 4;
   if (inv) extra += (size_t)(2 * D + H) * 4;

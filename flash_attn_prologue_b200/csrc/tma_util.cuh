@@ -6,6 +6,7 @@
 // GPU. flash_prologue_device_error() reads (and optionally clears) the word.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -79,6 +80,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1], %2, [%3], %4;"
       ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Tiled TMA load of a 5-D box (no multicast) completing on `bar`, with an L2
+// cache policy. c0 is the innermost coordinate: its byte offset must be a
+// multiple of 16 (the prologue kernels always pass 0). The shared-memory
+// destination is 128-byte aligned.
+__device__ __forceinline__ void tma_load_5d_hint(void* dst, const CUtensorMap* map, int32_t c0,
+                                                 int32_t c1, int32_t c2, int32_t c3, int32_t c4,
+                                                 uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+        "r"(c3), "r"(c4), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 
