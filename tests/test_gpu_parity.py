@@ -309,6 +309,33 @@ def test_bulk_copy_and_register_paths_agree(layout, d):
     assert rel_err(g0[2], g1[2]) < 1e-5 and rel_err(g0[3], g1[3]) < 1e-5
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_broadcast_upstream_gradients(d):
+    """Upstream gradients broadcast along tokens (stride 0, e.g. the gradient of a
+    sum over tokens) are read in place and give the bits of the materialised
+    gradient; the partially broadcast ones are read by the TMA path's fallback."""
+    h, t = 4, 200
+    g = torch.Generator(device="cuda").manual_seed(21 + d)
+    q, k = (torch.randn(t, h, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(2))
+    ang = torch.randn(t, d // 2, generator=g, device="cuda")
+    w = 1 + 0.2 * torch.randn(2, 1, d, generator=g, device="cuda")
+    s = 0.2 * torch.randn(h, 1, 1, generator=g, device="cuda")
+    args = (q, k, w, s, ang.sin(), ang.cos())
+    gq_row = torch.randn(1, h, d, generator=g, device="cuda").to(torch.bfloat16)
+    gk_row = torch.randn(1, h, d, generator=g, device="cuda").to(torch.bfloat16)
+    for gq, gk in ((gq_row.expand(t, h, d), gk_row.expand(t, h, d)),
+                   (gq_row[:, :1].expand(t, h, d), gk_row[:, :1].expand(t, h, d))):
+        got, ref = [], []
+        for grads, sink in (((gq, gk), got), ((gq.contiguous(), gk.contiguous()), ref)):
+            a = [x.detach().requires_grad_(i < 4) for i, x in enumerate(args)]
+            out = qknorm_rope_scale(*a, backend="cute")
+            sink.extend(torch.autograd.grad(out, a[:4], grads))
+        assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1])
+        assert rel_err(got[2], ref[2]) < 1e-5 and rel_err(got[3], ref[3]) < 1e-5
+    from flash_attn_prologue_b200 import _lib
+    assert _lib.device_error(reset=True) == 0
+
+
 def test_no_device_wait_timeouts():
     from flash_attn_prologue_b200 import _lib
     assert _lib.device_error(reset=True) == 0
