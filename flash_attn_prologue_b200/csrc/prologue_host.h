@@ -58,6 +58,9 @@ constexpr int kTmaTileBytes = 8192;                        // per streamed tenso
 __host__ __device__ constexpr int tma_stage_bytes(int nt, int table_bytes) {
   return (nt * kTmaTileBytes + 2 * table_bytes + 127) & ~127;
 }
+// The forward that saves r adds, after each stage's tables, the tile's r values
+// ([tensor][row], FP32) that the producer writes out once the stage is free.
+__host__ __device__ constexpr int tma_r_area_bytes(int rows) { return (2 * rows * 4 + 127) & ~127; }
 
 // The backward kernel runs the 8 consumer warps (warpgroups 0-1) beside a
 // whole producer warpgroup (warp 8 issues the copies; warps 9-11 leave once

@@ -102,6 +102,32 @@ __device__ __forceinline__ void lds_f8(float (&v)[kChunk], const unsigned char* 
 
 }  // namespace
 
+// Forward that saves r: one tile's r values, staged by the consumers in the
+// stage's r area ([tensor][row]), written by the producer warp to rms[t]
+// ([B, H, N] FP32) with consecutive lanes on consecutive positions, so a warp
+// store covers whole runs of a head's positions instead of one value per row.
+template <int ROWS>
+__device__ __forceinline__ void store_tile_r(const TmaFwdArgs& a, const TileCoords& tc,
+                                             const float* r_s, int lane) {
+  const int log2_to = __ffs(ROWS) - 1 - a.p.log2_ti;  // ti * to == ROWS, both powers of two
+  for (int idx = lane; idx < 2 * ROWS; idx += 32) {
+    const int t = idx >= ROWS;
+    const int q = idx - t * ROWS;
+    int i, o;  // inner / outer row index within the tile
+    if (a.p.heads_inner) {
+      o = q & ((1 << log2_to) - 1);
+      i = q >> log2_to;
+    } else {
+      i = q & (a.p.ti - 1);
+      o = q >> a.p.log2_ti;
+    }
+    if (o >= tc.vo || i >= tc.vi) continue;
+    const int64_t h = a.p.heads_inner ? tc.i0 + i : tc.o0 + o;
+    const int64_t n = a.p.heads_inner ? (int64_t)tc.o0 + o : (int64_t)tc.i0 + i;
+    a.rms[t][((int64_t)tc.b * a.H + h) * a.N + n] = r_s[t * ROWS + (o << a.p.log2_ti) + i];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Forward. RMS = true also stores each row's r to a.rms (inverse formulation).
 template <typename T, int D, bool RMS>
@@ -113,7 +139,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   extern __shared__ __align__(128) unsigned char smem[];
   const int S = a.p.stages;
   const int table_bytes = a.p.P * HALF * 4;
-  const int stage_bytes = tma_stage_bytes(2, table_bytes);
+  const int r_off = tma_stage_bytes(2, table_bytes);  // RMS: the tile's r values
+  const int stage_bytes = r_off + (RMS ? tma_r_area_bytes(S_::ROWS) : 0);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
   uint64_t* empty = full + S;
   float* w_s = reinterpret_cast<float*>(empty + S);
@@ -137,17 +164,33 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_table = policy_evict_last();
     int k = 0;
+    bool failed = false;
+    Cursor4 lag;  // RMS: the tile whose r values go out next, S tiles behind
+    lag.init(blockIdx.x, a.p.radix);
     for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {
       const int s = k % S;
-      if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
-      const TileCoords tc = tile_coords(a.p, cur);
+      if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) { failed = true; break; }
       unsigned char* st = smem + s * stage_bytes;
+      if (RMS && k >= S) {  // the consumers are done with tile k - S
+        store_tile_r<S_::ROWS>(a, tile_coords(a.p, lag), reinterpret_cast<const float*>(st + r_off), lane);
+        lag.advance(a.p.radix);
+      }
+      const TileCoords tc = tile_coords(a.p, cur);
       const int64_t n_first = a.p.heads_inner ? (int64_t)tc.o0 : (int64_t)tc.i0;
       const int np = a.p.heads_inner ? tc.vo : tc.vi;
       if (lane == 0) mbar_arrive_expect_tx(&full[s], 2 * kTmaTileBytes + 2 * np * HALF * 4);
       __syncwarp();
       issue_stage<D>(a.in, 2, a.sin, a.cos, a.sin_b, a.cos_b, n_first, np, tc, st, table_bytes,
                      &full[s], lane, pol_stream, pol_table);
+    }
+    if (RMS && !failed) {  // r of the last (up to S) tiles, once their stages are released
+      for (int j = k > S ? k - S : 0; j < k; ++j) {
+        const int s = j % S;
+        if (!mbar_wait(&empty[s], (j / S) & 1)) break;
+        store_tile_r<S_::ROWS>(a, tile_coords(a.p, lag),
+                               reinterpret_cast<const float*>(smem + s * stage_bytes + r_off), lane);
+        lag.advance(a.p.radix);
+      }
     }
     return;
   }
@@ -192,10 +235,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       lds_f8(sn, sin_s + (p_l * HALF + j0) * 4);
       lds_f8(cs, cos_s + (p_l * HALF + j0) * 4);
       const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
-      if (RMS && c == 0) {
-        const int64_t n = a.p.heads_inner ? (int64_t)tc.o0 + o_l : (int64_t)tc.i0 + i_l;
-        a.rms[t][((int64_t)tc.b * a.H + h) * a.N + n] = rr;
-      }
+      if (RMS && c == 0) reinterpret_cast<float*>(const_cast<unsigned char*>(st) + r_off)[t * S_::ROWS + r] = rr;
       Chunk<T> out1, out2;
       fwd_lane(x1, x2, rr, wa, wb, sn, cs, t == 0, t == 0 ? e_s[h] : 1.f, out1, out2);
       T* yp = ytile + (int64_t)i_l * so_inner + (int64_t)o_l * so_outer;
@@ -474,7 +514,8 @@ cudaError_t read_device_error(int* value, bool reset) {
 }
 
 size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv) {
-  const size_t stage = (size_t)tma_stage_bytes(n_tensors, p.P * (D / 2) * 4);
+  size_t stage = (size_t)tma_stage_bytes(n_tensors, p.P * (D / 2) * 4);
+  if (n_tensors == 2 && inv) stage += (size_t)tma_r_area_bytes(p.ti * p.to);
   size_t extra = (size_t)2 * p.stages * sizeof(uint64_t) + (size_t)(2 * D + H) * 4;
   if (n_tensors == 4) extra += (size_t)(4 * H + 8 * D) * 4;
   if (inv) extra += (size_t)(2 * D + H) * 4;
@@ -547,7 +588,7 @@ int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype, bool inv) 
 cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream) {
   const void* fn = tma_kernel_for(false, dtype, D, a.rms[0] != nullptr);
   if (!fn) return cudaErrorInvalidValue;
-  const size_t smem = tma_smem_bytes(a.p, D, 2, a.H);
+  const size_t smem = tma_smem_bytes(a.p, D, 2, a.H, a.rms[0] != nullptr);
   cudaError_t err = prepare_kernel(fn, smem);
   if (err != cudaSuccess) return err;
   const int64_t grid = persistent_grid(fn, smem, a.p.n_tiles, kTmaThreads);
