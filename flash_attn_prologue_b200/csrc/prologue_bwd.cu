@@ -23,7 +23,7 @@
 //
 // INV = true is the inverse backward (fused_epilogue.py:2200-2300): x[] hold the
 // forward outputs and rms[] the saved r of every row; the normalised row n is
-// rebuilt from them (inv_lane_normed) instead of being recomputed from q and k.
+// rebuilt from them (inv_lane_reduce) instead of being recomputed from q and k.
 #include "prologue_host.h"
 
 namespace flash_prologue {
@@ -117,19 +117,18 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
         for (int k = 0; k < Chunk<T>::kWords; ++k) { x1.w[k] = 0; x2.w[k] = 0; g1.w[k] = 0; g2.w[k] = 0; }
       }
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
-      float2 dnw1[kPairs], dnw2[kPairs];  // INV: dn w; otherwise u = d0 w
-      float2 n1[kPairs], n2[kPairs];  // INV: the rebuilt normalised row
-      float r, re = 0.f, dsum;
+      float2 dnw1[kPairs], dnw2[kPairs];  // u = d0 w (INV: t = d0 w)
+      float2 n1[kPairs], n2[kPairs];      // INV: n' = e n, rebuilt from the outputs
+      float r, re, dsum;
       if constexpr (INV) {
         r = ok ? __ldg(rms + (b * a.H + h) * a.N + n) : 0.f;
+        re = __fmul_rn(r, e);
+        float part = 0.f;
         if (ok) {
-          inv_lane_normed(x1, x2, t == 0, ie_s[h], iw + j0, iw + HALF + j0, sn, cs, n1, n2);
-        } else {
-#pragma unroll
-          for (int q = 0; q < kPairs; ++q) { n1[q] = make_float2(0.f, 0.f); n2[q] = n1[q]; }
+          part = inv_lane_reduce(x1, x2, g1, g2, w + j0, w + HALF + j0, iw + j0, iw + HALF + j0, sn,
+                                 cs, acc1p, acc2p, n1, n2, dnw1, dnw2);
         }
-        dsum = row_sum<L>(bwd_lane_reduce_n(n1, n2, g1, g2, e, t == 0, w + j0, w + HALF + j0, sn, cs,
-                                            acc1p, acc2p, dnw1, dnw2));
+        dsum = row_sum<L>(part);
       } else {
         r = inv_rms_bwd<D>(row_sum<L>(lane_sumsq2(x1, x2)), a.eps);
         re = __fmul_rn(r, e);
@@ -146,7 +145,9 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
       if (!ok) continue;
       Chunk<T> out1, out2;
       if constexpr (INV)
-        bwd_lane_dx_n<T>(n1, n2, r, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
+        inv_lane_dx<T>(n1, n2, dnw1, dnw2, re,
+                       __fmul_rn(__fmul_rn(r, dsum * (1.0f / (float)D)), t == 0 ? ie_s[h] : 1.f),
+                       out1, out2);
       else
         bwd_lane_dx(x1, x2, re, __fmul_rn(r, __fmul_rn(r, dsum * (1.0f / (float)D))), dnw1, dnw2,
                     out1, out2);

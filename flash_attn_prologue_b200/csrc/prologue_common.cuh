@@ -399,69 +399,61 @@ __device__ __forceinline__ void bwd_lane_dx(const Chunk<T>& x1, const Chunk<T>& 
 // ---------------------------------------------------------------------------
 // Inverse backward (the outputs and r are saved instead of the inputs; the
 // reference's qknorm_rope_scale_cute_inverse_backward,
-// flash_attn_prologue/fused_epilogue.py:2200-2300). The normalised row of one
-// lane is rebuilt from the forward output o: u = o / e (Q only), the inverse
-// rotation m = R^T u, n = m / w. The divisions are multiplications by the
-// reciprocals ie = 1/e and iw = 1/w (each rounded once).
+// flash_attn_prologue/fused_epilogue.py:2200-2300). The forward output of a row
+// is o = e R(n w), so m0 = R^T o = e n w and n' = m0 / w = e n (1/w is the
+// precomputed reciprocal iw). With d0 = R^T g, the gradient of n w is
+// dy = e d0, so
+//   d w partial:  acc += d0 * n'                       (= dy n)
+//   returned:     lane partial of sum_j d0_j m0_j      (= <dy w, n> = <dn, n>, and
+//                 <R^T g, R^T o> = sum_j dq_out_j q_out_j: the d scale term)
+// The lane keeps n' and t = d0 w for the dx part. Two independent partial sums
+// (first / second half) shorten the dependency chain.
 template <typename T>
-__device__ __forceinline__ void inv_lane_normed(const Chunk<T>& o1, const Chunk<T>& o2, bool scale,
-                                                float ie, const float* iwa, const float* iwb,
-                                                const float (&sn)[kChunk], const float (&cs)[kChunk],
-                                                float2 (&n1)[kPairs], float2 (&n2)[kPairs]) {
-  const float2 ie2 = splat2(ie);
+__device__ __forceinline__ float inv_lane_reduce(const Chunk<T>& o1, const Chunk<T>& o2,
+                                                 const Chunk<T>& g1, const Chunk<T>& g2,
+                                                 const float* wa, const float* wb, const float* iwa,
+                                                 const float* iwb, const float (&sn)[kChunk],
+                                                 const float (&cs)[kChunk], float2 (&acc1)[kPairs],
+                                                 float2 (&acc2)[kPairs], float2 (&np1)[kPairs],
+                                                 float2 (&np2)[kPairs], float2 (&t1)[kPairs],
+                                                 float2 (&t2)[kPairs]) {
+  float2 ds1 = make_float2(0.f, 0.f), ds2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int p = 0; p < kPairs; ++p) {
     const float2 c2 = make_float2(cs[2 * p], cs[2 * p + 1]);
     const float2 s2 = make_float2(sn[2 * p], sn[2 * p + 1]);
-    float2 u1 = chunk_get2(o1, p), u2 = chunk_get2(o2, p);
-    if (scale) { u1 = __fmul2_rn(u1, ie2); u2 = __fmul2_rn(u2, ie2); }
-    const float2 m1 = __fadd2_rn(__fmul2_rn(u1, c2), __fmul2_rn(u2, s2));
-    const float2 m2 = __fadd2_rn(__fmul2_rn(u2, c2), neg2(__fmul2_rn(u1, s2)));
-    n1[p] = __fmul2_rn(m1, ld_pair(iwa, p));
-    n2[p] = __fmul2_rn(m2, ld_pair(iwb, p));
-  }
-}
-
-// bwd_lane_reduce with the normalised row n given instead of x and r.
-template <typename T>
-__device__ __forceinline__ float bwd_lane_reduce_n(const float2 (&n1)[kPairs], const float2 (&n2)[kPairs],
-                                                   const Chunk<T>& g1, const Chunk<T>& g2, float e,
-                                                   bool scale, const float* wa, const float* wb,
-                                                   const float (&sn)[kChunk], const float (&cs)[kChunk],
-                                                   float2 (&acc1)[kPairs], float2 (&acc2)[kPairs],
-                                                   float2 (&dnw1)[kPairs], float2 (&dnw2)[kPairs]) {
-  const float2 e2 = splat2(e);
-  float2 dsum = make_float2(0.f, 0.f);
-#pragma unroll
-  for (int p = 0; p < kPairs; ++p) {
-    const float2 c2 = make_float2(cs[2 * p], cs[2 * p + 1]);
-    const float2 s2 = make_float2(sn[2 * p], sn[2 * p + 1]);
-    float2 ga = chunk_get2(g1, p), gb = chunk_get2(g2, p);
-    if (scale) { ga = __fmul2_rn(ga, e2); gb = __fmul2_rn(gb, e2); }
+    const float2 oa = chunk_get2(o1, p), ob = chunk_get2(o2, p);
+    const float2 ga = chunk_get2(g1, p), gb = chunk_get2(g2, p);
+    const float2 m1 = __ffma2_rn(oa, c2, __fmul2_rn(ob, s2));
+    const float2 m2 = __ffma2_rn(ob, c2, neg2(__fmul2_rn(oa, s2)));
     const float2 d1 = __ffma2_rn(ga, c2, __fmul2_rn(gb, s2));
     const float2 d2 = __ffma2_rn(gb, c2, neg2(__fmul2_rn(ga, s2)));
-    acc1[p] = __ffma2_rn(d1, n1[p], acc1[p]);
-    acc2[p] = __ffma2_rn(d2, n2[p], acc2[p]);
-    dnw1[p] = __fmul2_rn(d1, ld_pair(wa, p));
-    dnw2[p] = __fmul2_rn(d2, ld_pair(wb, p));
-    dsum = __ffma2_rn(dnw1[p], n1[p], dsum);
-    dsum = __ffma2_rn(dnw2[p], n2[p], dsum);
+    np1[p] = __fmul2_rn(m1, ld_pair(iwa, p));
+    np2[p] = __fmul2_rn(m2, ld_pair(iwb, p));
+    acc1[p] = __ffma2_rn(d1, np1[p], acc1[p]);
+    acc2[p] = __ffma2_rn(d2, np2[p], acc2[p]);
+    t1[p] = __fmul2_rn(d1, ld_pair(wa, p));
+    t2[p] = __fmul2_rn(d2, ld_pair(wb, p));
+    ds1 = __ffma2_rn(d1, m1, ds1);
+    ds2 = __ffma2_rn(d2, m2, ds2);
   }
-  return __fadd_rn(dsum.x, dsum.y);
+  const float2 ds = __fadd2_rn(ds1, ds2);
+  return __fadd_rn(ds.x, ds.y);
 }
 
-// bwd_lane_dx with the normalised row n given.
+// Inverse backward, dx of one lane: dx = r (dn - n m) with dn = e t, n = n' / e
+// and m = <dn, n> / D, evaluated as re * t - n' * kx with re = r e and
+// kx = r m / e.
 template <typename T>
-__device__ __forceinline__ void bwd_lane_dx_n(const float2 (&n1)[kPairs], const float2 (&n2)[kPairs],
-                                              float r, float m, const float2 (&dnw1)[kPairs],
-                                              const float2 (&dnw2)[kPairs], Chunk<T>& out1,
-                                              Chunk<T>& out2) {
-  const float2 r2 = splat2(r), nm2 = splat2(-m);
+__device__ __forceinline__ void inv_lane_dx(const float2 (&np1)[kPairs], const float2 (&np2)[kPairs],
+                                            const float2 (&t1)[kPairs], const float2 (&t2)[kPairs],
+                                            float re, float kx, Chunk<T>& out1, Chunk<T>& out2) {
+  const float2 re2 = splat2(re), nk2 = splat2(-kx);
   float2 o1[kPairs], o2[kPairs];
 #pragma unroll
   for (int p = 0; p < kPairs; ++p) {
-    o1[p] = __fmul2_rn(r2, __ffma2_rn(n1[p], nm2, dnw1[p]));
-    o2[p] = __fmul2_rn(r2, __ffma2_rn(n2[p], nm2, dnw2[p]));
+    o1[p] = __ffma2_rn(np1[p], nk2, __fmul2_rn(re2, t1[p]));
+    o2[p] = __ffma2_rn(np2[p], nk2, __fmul2_rn(re2, t2[p]));
   }
   chunk_set2(out1, o1);
   chunk_set2(out2, o2);

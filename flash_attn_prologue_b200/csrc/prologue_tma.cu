@@ -396,19 +396,18 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       }
       const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
-      float2 dnw1[kPairs], dnw2[kPairs];  // INV: dn w; otherwise u = d0 w
-      float2 n1[kPairs], n2[kPairs];  // INV: the rebuilt normalised row
-      float rr, re = 0.f, dsum;
+      float2 dnw1[kPairs], dnw2[kPairs];  // u = d0 w (INV: t = d0 w)
+      float2 n1[kPairs], n2[kPairs];      // INV: n' = e n, rebuilt from the outputs
+      float rr, re, dsum;
       if constexpr (INV) {
         rr = pass == 0 ? rv0 : rv1;
+        re = __fmul_rn(rr, e);
+        float part = 0.f;
         if (ok) {
-          inv_lane_normed(x1, x2, t == 0, ie_s[h], iwa, iwb, sn, cs, n1, n2);
-        } else {
-#pragma unroll
-          for (int q = 0; q < kPairs; ++q) { n1[q] = make_float2(0.f, 0.f); n2[q] = n1[q]; }
+          part = inv_lane_reduce(x1, x2, g1, g2, wa, wb, iwa, iwb, sn, cs, acc1p, acc2p, n1, n2, dnw1,
+                                 dnw2);
         }
-        dsum = row_sum<L>(bwd_lane_reduce_n(n1, n2, g1, g2, e, t == 0, wa, wb, sn, cs, acc1p, acc2p,
-                                            dnw1, dnw2));
+        dsum = row_sum<L>(part);
       } else {
         rr = inv_rms_bwd<D>(row_sum<L>(lane_sumsq2(x1, x2)), a.eps);
         re = __fmul_rn(rr, e);
@@ -424,7 +423,9 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       if (!ok) continue;
       Chunk<T> out1, out2;
       if constexpr (INV)
-        bwd_lane_dx_n<T>(n1, n2, rr, dsum * (1.0f / (float)D), dnw1, dnw2, out1, out2);
+        inv_lane_dx<T>(n1, n2, dnw1, dnw2, re,
+                       __fmul_rn(__fmul_rn(rr, dsum * (1.0f / (float)D)), t == 0 ? ie_s[h] : 1.f),
+                       out1, out2);
       else
         bwd_lane_dx(x1, x2, re, __fmul_rn(rr, __fmul_rn(rr, dsum * (1.0f / (float)D))), dnw1, dnw2,
                     out1, out2);
