@@ -154,6 +154,14 @@ def test_lazy_exports_resolve_to_ops_in_any_order():
     (``fused_qkv`` is also a submodule name); gemm_bwd keeps the reference's module path."""
     import subprocess
     import sys
+    first = (
+        "import flash_attn_prologue_b200 as f\n"
+        "import flash_attn_prologue_b200.fused_qkv\n"
+        "assert 'CustomOpDef' in repr(f.fused_qkv), repr(f.fused_qkv)\n"
+        "from flash_attn_prologue_b200.fused_qkv import fused_qkv_op\n"
+        "assert f.fused_qkv is fused_qkv_op\n"
+    )
+    subprocess.run([sys.executable, "-c", first], check=True, cwd=ROOT)
     code = (
         "import flash_attn_prologue_b200 as f\n"
         "a = f.matmul_bwd_dx\n"
