@@ -348,15 +348,17 @@ __device__ __forceinline__ void fwd_lane(const Chunk<T>& x1, const Chunk<T>& x2,
 //   returned:     lane partial of sum_j u_j (x_j re)        (= <dn, n>)
 // and u is kept for the dx part. The returned sum is also the row's
 // contribution to d scale: <dn, n> = <R^T g', n w> = <g', R(n w)> =
-// sum_j dq_out_j q_out_j. Two independent partial sums (first / second half)
-// shorten the dependency chain.
+// sum_j dq_out_j q_out_j. The lane keeps n' = x re for the dx part (lane_dx),
+// so x is not unpacked again. Two independent partial sums (first / second
+// half) shorten the dependency chain.
 template <typename T>
 __device__ __forceinline__ float bwd_lane_reduce(const Chunk<T>& x1, const Chunk<T>& x2,
                                                  const Chunk<T>& g1, const Chunk<T>& g2, float re,
                                                  const float* wa, const float* wb,
                                                  const float (&sn)[kChunk], const float (&cs)[kChunk],
                                                  float2 (&acc1)[kPairs], float2 (&acc2)[kPairs],
-                                                 float2 (&u1)[kPairs], float2 (&u2)[kPairs]) {
+                                                 float2 (&u1)[kPairs], float2 (&u2)[kPairs],
+                                                 float2 (&nx1)[kPairs], float2 (&nx2)[kPairs]) {
   const float2 re2 = splat2(re);
   float2 ds1 = make_float2(0.f, 0.f), ds2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -368,6 +370,8 @@ __device__ __forceinline__ float bwd_lane_reduce(const Chunk<T>& x1, const Chunk
     const float2 d2 = __ffma2_rn(gb, c2, neg2(__fmul2_rn(ga, s2)));
     const float2 n1 = __fmul2_rn(chunk_get2(x1, p), re2);
     const float2 n2 = __fmul2_rn(chunk_get2(x2, p), re2);
+    nx1[p] = n1;
+    nx2[p] = n2;
     acc1[p] = __ffma2_rn(d1, n1, acc1[p]);
     acc2[p] = __ffma2_rn(d2, n2, acc2[p]);
     u1[p] = __fmul2_rn(d1, ld_pair(wa, p));
@@ -377,23 +381,6 @@ __device__ __forceinline__ float bwd_lane_reduce(const Chunk<T>& x1, const Chunk
   }
   const float2 ds = __fadd2_rn(ds1, ds2);
   return __fadd_rn(ds.x, ds.y);
-}
-
-// Backward, dx of one lane: dx = r (dn - n m) with dn = e u, n = x r and
-// m = <dn, n> / D, evaluated as re * u - x * kx with kx = r * r * m.
-template <typename T>
-__device__ __forceinline__ void bwd_lane_dx(const Chunk<T>& x1, const Chunk<T>& x2, float re, float kx,
-                                            const float2 (&u1)[kPairs], const float2 (&u2)[kPairs],
-                                            Chunk<T>& out1, Chunk<T>& out2) {
-  const float2 re2 = splat2(re), nk2 = splat2(-kx);
-  float2 o1[kPairs], o2[kPairs];
-#pragma unroll
-  for (int p = 0; p < kPairs; ++p) {
-    o1[p] = __ffma2_rn(chunk_get2(x1, p), nk2, __fmul2_rn(re2, u1[p]));
-    o2[p] = __ffma2_rn(chunk_get2(x2, p), nk2, __fmul2_rn(re2, u2[p]));
-  }
-  chunk_set2(out1, o1);
-  chunk_set2(out2, o2);
 }
 
 // ---------------------------------------------------------------------------
@@ -441,11 +428,12 @@ __device__ __forceinline__ float inv_lane_reduce(const Chunk<T>& o1, const Chunk
   return __fadd_rn(ds.x, ds.y);
 }
 
-// Inverse backward, dx of one lane: dx = r (dn - n m) with dn = e t, n = n' / e
+// Backward (both formulations), dx of one lane: dx = r (dn - n m) with
+// dn = e t (t = d0 w), n = n' / e (n' = e n: x re, or rebuilt from the outputs)
 // and m = <dn, n> / D, evaluated as re * t - n' * kx with re = r e and
 // kx = r m / e.
 template <typename T>
-__device__ __forceinline__ void inv_lane_dx(const float2 (&np1)[kPairs], const float2 (&np2)[kPairs],
+__device__ __forceinline__ void lane_dx(const float2 (&np1)[kPairs], const float2 (&np2)[kPairs],
                                             const float2 (&t1)[kPairs], const float2 (&t2)[kPairs],
                                             float re, float kx, Chunk<T>& out1, Chunk<T>& out2) {
   const float2 re2 = splat2(re), nk2 = splat2(-kx);
