@@ -101,7 +101,7 @@ def load():
 
 
 def set_path(mode: int) -> None:
-    """0: bulk-copy pipeline when the layout allows (default); 1: register path only."""
+    """0: TMA pipeline when the layout allows (default); 1: register path only."""
     check(load().flash_prologue_set_path(int(mode)), "flash_prologue_set_path")
 
 

@@ -194,7 +194,7 @@ int common_checks(const void* q, const int64_t* qs, const void* k, const int64_t
   return st;
 }
 
-// 0: automatic (bulk-copy pipeline when the layout allows it), 1: register path only.
+// 0: automatic (TMA pipeline when the layout allows it), 1: register path only.
 int g_path_mode = 0;
 
 constexpr int kFwdStages = 3;
@@ -227,7 +227,7 @@ bool tma_tensor_ok(const void* p, const int64_t s[4], int64_t B, int64_t D, int 
   return encode_tensor_map(&out->map, type, 5, p, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-// sin/cos tables the bulk-copy path can read: rows of D/2 contiguous floats.
+// sin/cos tables the TMA path can read (bulk copies): rows of D/2 contiguous floats.
 bool tma_table_ok(const float* p, const int64_t s[3], int64_t N, int64_t D) {
   if (!aligned16(p) || s[2] != 1) return false;
   if (N > 1 && s[1] != D / 2) return false;

@@ -239,7 +239,7 @@ __device__ __forceinline__ float inv_rms_bwd(float sumsq, float eps) {
 }
 
 // ---------------------------------------------------------------------------
-// Per-row arithmetic shared by the register-path and the bulk-copy kernels (so
+// Per-row arithmetic shared by the register-path and the TMA kernels (so
 // both give bit-identical results). A lane holds the chunk pair
 // x1 = x[j0 .. j0+8), x2 = x[D/2+j0 .. D/2+j0+8) of its row and works on
 // element pairs (2p, 2p+1) with sm_100's paired FP32 instructions

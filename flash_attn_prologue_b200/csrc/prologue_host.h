@@ -48,7 +48,7 @@ struct BwdArgs {
 };
 
 // ---------------------------------------------------------------------------
-// Bulk-copy (TMA) pipelined path.
+// TMA pipelined path.
 constexpr int kTmaConsumerWarps = 8;                       // 0-3: Q rows, 4-7: K rows
 constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kTmaTileBytes = 8192;                        // per streamed tensor per stage
@@ -132,7 +132,7 @@ struct TmaBwdArgs {
 
 TmaPlan plan_tma(int64_t B, int64_t H, int64_t N, int D, int dtype, bool heads_inner, int stages);
 size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv = false);
-// Read (synchronously) and optionally clear the error words of the bulk-copy
+// Read (synchronously) and optionally clear the error words of the TMA
 // prologue kernels, of the fused QKV GEMM and of its backward GEMMs.
 cudaError_t read_device_error(int* value, bool reset);
 cudaError_t read_gemm_device_error(int* value, bool reset);

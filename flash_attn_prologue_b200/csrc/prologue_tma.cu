@@ -1,4 +1,4 @@
-// Bulk-copy (TMA) pipelined forward and backward prologue kernels.
+// TMA pipelined forward and backward prologue kernels.
 //
 // CTA = 8 consumer warps + 1 producer warp, two CTAs per SM (the backward CTA
 // has a whole producer warpgroup, which hands its registers to the consumers:

@@ -1,4 +1,4 @@
-// Bulk-copy (TMA) and mbarrier helpers for sm_100a, written as inline PTX.
+// TMA (bulk and tensor copies) and mbarrier helpers for sm_100a, written as inline PTX.
 //
 // Every wait is bounded: after kMaxWaitTries suspended polls (a few seconds in
 // total) the waiter records kDeviceErrorTimeout in the library's device error

@@ -304,9 +304,10 @@ FLASH_PROLOGUE_API int flash_prologue_bwd_noalloc(const void* q, const int64_t q
 
 /*
  * Kernel path selection (process-wide, not thread-safe; for tests and tuning).
- * mode 0 (default): the bulk-copy (TMA) pipelined kernels whenever the views
- * allow them (16-byte aligned, rows contiguous along the inner row dim, sin/cos
- * rows contiguous), else the register-path kernels; mode 1: register path
+ * mode 0 (default): the TMA pipelined kernels whenever the views
+ * allow them (16-byte aligned, rows contiguous along the inner row dim, positive
+ * 16-byte-multiple outer strides, sin/cos rows contiguous, a tensor map the
+ * driver accepts), else the register-path kernels; mode 1: register path
  * only. Both paths compute bit-identical results.
  * No counterpart in the reference (which has a single kernel per op).
  */

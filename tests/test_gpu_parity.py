@@ -263,7 +263,7 @@ def test_backward_bit_reproducible():
 
 
 # ----------------------------------------------------------------------------
-# The two kernel paths (bulk-copy pipeline and register path) compute the same
+# The two kernel paths (TMA pipeline and register path) compute the same
 # per-row arithmetic: outputs and dq/dk must be bit-identical; the parameter
 # gradients differ only in the (fixed) grouping of their partial sums.
 

@@ -92,7 +92,7 @@ def test_packed_strided_qkv_views_both_paths():
     _, _, w, s, sin, cos, gq, gk = (t.cuda() for t in _problem(1, H, T, D, seed=8))
     results = []
     try:
-        for mode in (0, 1):  # bulk-copy pipeline, register path
+        for mode in (0, 1):  # TMA pipeline, register path
             _lib.set_path(mode)
             results.append(_check_inverse(q, k, w, s, sin, cos, gq, gk))
     finally:
