@@ -6,8 +6,6 @@ callables are exported lazily under the reference's names, so importing the
 package touches neither CUDA nor the shared library, and changes no
 environment variable.
 """
-import sys as _sys
-import types as _types
 from importlib import import_module
 
 from .functional import prepare_backend, qknorm_rope_scale, qknorm_rope_scale_qkv
@@ -49,21 +47,3 @@ def __getattr__(name):
         if mod is not None:
             globals()[alias] = getattr(mod, exported)
     return globals()[name]
-
-
-class _Package(_types.ModuleType):
-    """The package module, keeping the op aliases when a submodule of the same
-    name is imported: the import system binds the package attribute
-    ``fused_qkv`` to the submodule ``fused_qkv`` when it loads, while the
-    package exports the op under that name. Such a binding is replaced by the
-    op, so ``fused_qkv`` is the op however the submodule was imported."""
-
-    def __setattr__(self, name, value):
-        if isinstance(value, _types.ModuleType) and name in _LAZY:
-            source, exported = _LAZY[name]
-            if value.__name__ == f"{__name__}.{source}":
-                value = getattr(value, exported)
-        super().__setattr__(name, value)
-
-
-_sys.modules[__name__].__class__ = _Package

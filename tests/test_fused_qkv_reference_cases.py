@@ -11,8 +11,10 @@ rmsnorm_weight (rtol 1e-2, atol 1e-1) and scales (rtol 1e-2, atol 6.0).
 import pytest
 import torch
 
-import flash_attn_prologue_b200.fused_qkv  # noqa: F401  (registers the fused QKV ops)
+import flash_attn_prologue_b200 as fap
 from flash_attn_prologue_b200 import prepare_backend
+
+fap.fused_qkv_epilogue  # noqa: B018  (the lazy export loads and registers the fused QKV ops)
 
 pytestmark = pytest.mark.gpu
 OPS = torch.ops.flash_prologue
