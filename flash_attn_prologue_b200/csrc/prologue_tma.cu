@@ -19,8 +19,10 @@
 // The arithmetic per row is the one of the register-path kernels
 // (prologue_fwd.cu / prologue_bwd.cu), in the same order, so both paths give
 // bit-identical results.
+#include <map>
 #include <mutex>
 #include <unordered_set>
+#include <utility>
 
 #include "prologue_host.h"
 #include "tma_util.cuh"
@@ -553,9 +555,28 @@ static const void* tma_kernel_for(bool bwd, int dtype, int D, bool inv) {
 #undef FP_TMA_CASE
 }
 
+// Opts the kernel in to `smem` bytes of dynamic shared memory on the current
+// device. The attribute is per device and only has to grow, so the call is made
+// once per (kernel, device) and larger size instead of on every launch.
 static cudaError_t prepare_kernel(const void* fn, size_t smem) {
-  // Opt in to more than 48 KB of dynamic shared memory (idempotent, cheap).
-  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> opted;
+  const auto key = std::make_pair(fn, dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = opted.find(key);
+    if (it != opted.end() && it->second >= smem) return cudaSuccess;
+  }
+  err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err == cudaSuccess) {
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& v = opted[key];
+    if (smem > v) v = smem;
+  }
+  return err;
 }
 
 // The backward kernel's register split (producer warpgroup down, consumers up)

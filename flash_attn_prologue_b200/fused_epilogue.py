@@ -189,14 +189,24 @@ def _qknorm_rope_scale_cute_fake(q, k, rmsnorm_weight, scales, sin, cos, eps=1e-
     )
 
 
+_WORKSPACE_BYTES = {}
+
+
 def bwd_workspace_bytes(B: int, H: int, N: int, D: int, dtype: torch.dtype) -> int:
-    """Device workspace (bytes) of the backward launch on the current device."""
+    """Device workspace (bytes) of the backward launch on the current device
+    (a pure function of the shape and the device, so it is queried once)."""
     import ctypes
-    nbytes = ctypes.c_size_t(0)
-    status = _lib.load().flash_prologue_bwd_workspace_size(B, H, N, D, _lib.DTYPE_CODES[dtype],
-                                                           ctypes.byref(nbytes))
-    _lib.check(status, "flash_prologue_bwd_workspace_size")
-    return int(nbytes.value)
+    key = (B, H, N, D, dtype, torch.cuda.current_device())
+    nbytes = _WORKSPACE_BYTES.get(key)
+    if nbytes is None:
+        out = ctypes.c_size_t(0)
+        status = _lib.load().flash_prologue_bwd_workspace_size(B, H, N, D, _lib.DTYPE_CODES[dtype],
+                                                               ctypes.byref(out))
+        _lib.check(status, "flash_prologue_bwd_workspace_size")
+        if len(_WORKSPACE_BYTES) >= 4096:  # many distinct shapes: start over
+            _WORKSPACE_BYTES.clear()
+        nbytes = _WORKSPACE_BYTES[key] = int(out.value)
+    return nbytes
 
 
 def _grad_view(g: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
