@@ -186,6 +186,15 @@ def test_empty_inputs_cuda():
 # ----------------------------------------------------------------------------
 # Full-size benchmark configurations.
 
+def _assert_band_budget(ok, stats):
+    """Full-size bar: every element within 1 BF16 ulp or the cancellation band,
+    > 99% bit-exact, and at most 1e-4 of the elements (1 in 10,000) outside
+    1 ulp -- the elements the band admits must stay rare."""
+    assert ok, stats
+    assert stats["exact_frac"] > 0.99, stats
+    assert stats["beyond_ulp_in_band"] <= 1e-4 * stats["elements"], stats
+
+
 def _rope(positions, d, theta):
     inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float64, device=positions.device) / d))
     ang = (positions.double()[:, None] * inv[None]).float()
@@ -211,8 +220,11 @@ def test_config2_full_size_sampled_rows_and_param_grads():
     sub = [x[idx].detach().cpu() for x in (q, k)]
     ref_out, ref_grads = native_forward_backward(sub[0], sub[1], w.cpu(), s.cpu(), sin[idx].cpu(),
                                                  cos[idx].cpu(), gq[idx].cpu(), gk[idx].cpu())
-    _check_outputs((out[0][idx], out[1][idx]), ref_out, torch.bfloat16,
-                   (sub[0], sub[1], w.cpu(), s.cpu(), sin[idx].cpu(), cos[idx].cpu()))
+    mags = term_magnitudes(sub[0], sub[1], w.cpu(), s.cpu(), sin[idx].cpu(), cos[idx].cpu())
+    for got, exp, mag, nm in zip((out[0][idx], out[1][idx]), ref_out, mags, ("q_out", "k_out")):
+        ok, stats = check_outputs(got.cpu(), exp, mag)
+        print(f"C2 sampled {nm}: {stats}")
+        _assert_band_budget(ok, stats)
     for got, exp in zip((grads[0][idx], grads[1][idx]), ref_grads[:2]):
         torch.testing.assert_close(got.cpu().float(), exp.float(), rtol=1e-2, atol=1e-2)
     # Whole-problem parameter gradients against the FP32 torch formulation.
@@ -235,9 +247,10 @@ def test_config3_full_size_dense():
     out = qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute")
     ref = native_forward(q, k, w, s, sin, cos)  # FP32 torch formulation on the GPU
     mags = term_magnitudes(q, k, w, s, sin, cos)
-    for got, exp, mag in zip(out, ref, mags):
+    for got, exp, mag, nm in zip(out, ref, mags, ("q_out", "k_out")):
         ok, stats = check_outputs(got, exp, mag)
-        assert ok and stats["exact_frac"] > 0.99, stats
+        print(f"C3 full {nm}: {stats}")
+        _assert_band_budget(ok, stats)
 
 
 def test_backward_bit_reproducible():

@@ -4,11 +4,14 @@ It serves callers that cannot allocate device memory per call (runtimes that
 plan all device memory up front, host-language bindings without a device
 allocator); its scratch is a static 1 MiB array inside the library. Checked
 here through the C ABI against the existing entry point (flash_prologue_bwd,
-reached through the flash_prologue::qknorm_rope_scale_cute_backward op), on two
-calls in a row with different inputs, so nothing left in the shared scratch by
-the first call can leak into the second; and for the rejection of a problem
-too large for the scratch. This file is collected last, so a run that stops at
-the first failure has run every other test before it.
+reached through the flash_prologue::qknorm_rope_scale_cute_backward op): both
+run the same kernels on the same grid, so every result must be bit-identical.
+Each kernel path (TMA pipeline and register path) runs a sequence of calls in a
+row with different inputs and grid sizes -- a large grid, then a small one, then
+the large one again -- so partial rows a previous call left in the shared
+scratch are present and must not leak into the next result; and a problem too
+large for the scratch is rejected. This file is collected last, so a run that
+stops at the first failure has run every other test before it.
 """
 import ctypes
 
@@ -17,23 +20,30 @@ import torch
 
 from flash_attn_prologue_b200 import _lib, prepare_backend
 from flash_attn_prologue_b200.fused_epilogue import _get_compact_strides
-from tests._util import rel_err
 
 pytestmark = pytest.mark.gpu
 
+# (T, H, D, packed): packed [T, H, D] views of a fused QKV buffer (heads inner),
+# or dense [1, H, T, D] tensors (positions inner). The first needs the full
+# persistent grid, the second a few dozen CTAs.
+SEQUENCE = [(4096, 8, 64, True), (300, 4, 128, True), (4096, 8, 64, True), (700, 2, 128, False)]
 
-def _problem(seed, T=4096, H=8, D=64):
+
+def _problem(seed, T, H, D, packed):
     g = torch.Generator(device="cuda").manual_seed(seed)
-    buf = torch.randn(T, 3, H, D, generator=g, device="cuda").to(torch.bfloat16)
-    q4 = buf[:, 0].permute(1, 0, 2)[None]
-    k4 = buf[:, 1].permute(1, 0, 2)[None]
+    if packed:
+        buf = torch.randn(T, 3, H, D, generator=g, device="cuda").to(torch.bfloat16)
+        q4 = buf[:, 0].permute(1, 0, 2)[None]
+        k4 = buf[:, 1].permute(1, 0, 2)[None]
+    else:
+        q4, k4 = (torch.randn(1, H, T, D, generator=g, device="cuda").to(torch.bfloat16) for _ in range(2))
     w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device="cuda")
     s = 0.1 * torch.randn(H, 1, 1, generator=g, device="cuda")
     ang = torch.randn(T, D // 2, generator=g, device="cuda")
     sin, cos = ang.sin(), ang.cos()
-    gq4 = torch.randn(T, H, D, generator=g, device="cuda").to(torch.bfloat16).permute(1, 0, 2)[None]
-    gk4 = torch.randn(T, H, D, generator=g, device="cuda").to(torch.bfloat16).permute(1, 0, 2)[None]
-    return buf, q4, k4, w, s, sin, cos, gq4, gk4
+    gq4, gk4 = (torch.randn(T, H, D, generator=g, device="cuda").to(torch.bfloat16).permute(1, 0, 2)[None]
+                for _ in range(2))
+    return q4, k4, w, s, sin, cos, gq4, gk4
 
 
 def _call_noalloc(q4, k4, w, s, sin, cos, gq4, gk4):
@@ -64,17 +74,20 @@ def _call_existing(q4, k4, w, s, sin, cos, gq4, gk4):
         q4, k4, w, s, sin4, cos4, gq4, gk4, 1e-5)
 
 
-def test_noalloc_backward_matches_workspace_backward_twice():
+@pytest.mark.parametrize("path", [0, 1], ids=["tma", "register"])
+def test_noalloc_backward_equals_workspace_backward(path):
     prepare_backend("cute")
-    for seed in (0, 1):  # two calls in a row, different inputs
-        args = _problem(seed)[1:]
-        got = _call_noalloc(*args)
-        ref = _call_existing(*args)
-        torch.cuda.synchronize()
-        for a, b in zip(got[:2], ref[:2]):
-            torch.testing.assert_close(a.float(), b.float(), rtol=1e-2, atol=1e-2)
-        assert rel_err(got[2], ref[2]) < 1e-3
-        assert rel_err(got[3], ref[3]) < 1e-3
+    try:
+        _lib.set_path(path)
+        for i, shape in enumerate(SEQUENCE):  # calls in a row: different inputs and grids
+            args = _problem(10 * path + i, *shape)
+            got = _call_noalloc(*args)
+            ref = _call_existing(*args)
+            torch.cuda.synchronize()
+            for a, b, nm in zip(got, ref, ("dq", "dk", "drmsnorm_weight", "dscales")):
+                assert a.shape == b.shape and torch.equal(a, b), (shape, nm)
+    finally:
+        _lib.set_path(0)
     assert _lib.device_error(reset=True) == 0
 
 
