@@ -97,8 +97,10 @@ FLASH_PROLOGUE_API int flash_prologue_copy_rows(const void* src, const int64_t s
   const int64_t want = (rows + rows_per_block - 1) / rows_per_block;
   const int64_t cap = 8LL * sms;
   const unsigned grid = (unsigned)(want < cap ? want : cap);
-  copy_rows_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  return cudaGetLastError() == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
+  return launch_kernel(copy_rows_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), a) ==
+                 cudaSuccess
+             ? FLASH_PROLOGUE_OK
+             : FLASH_PROLOGUE_ERR_CUDA;
 }
 
 }  // extern "C"

@@ -279,8 +279,8 @@ cudaError_t launch_bwd(const BwdArgs& a, float* dw, float* ds, int dtype, int D,
 
 cudaError_t launch_bwd_finalize(const float* partials, int64_t G, int C, int two_d, float* dw,
                                 float* ds, cudaStream_t stream) {
-  prologue_bwd_finalize_kernel<<<(C + 31) / 32, kThreads, 0, stream>>>(partials, G, C, two_d, dw, ds);
-  return cudaGetLastError();
+  return launch_kernel(prologue_bwd_finalize_kernel, dim3((C + 31) / 32), dim3(kThreads), 0, stream,
+                       partials, G, C, two_d, dw, ds);
 }
 
 }  // namespace flash_prologue

@@ -83,8 +83,8 @@ static cudaError_t launch_fwd_t(const FwdArgs& a, cudaStream_t stream) {
   if (grid <= 0) return cudaErrorInvalidConfiguration;
   FwdArgs args = a;
   args.g.radix = make_radix(2, a.g.n_pos_blocks, a.g.n_head_groups, grid);
-  prologue_fwd_kernel<T, D, VEC><<<(unsigned)grid, kThreads, smem, stream>>>(args);
-  return cudaGetLastError();
+  return launch_kernel(prologue_fwd_kernel<T, D, VEC>, dim3((unsigned)grid), dim3(kThreads), smem, stream,
+                       args);
 }
 
 template <typename T, int D>

@@ -6,9 +6,30 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <tuple>
+#include <type_traits>
+#include <utility>
+
 #include "prologue_common.cuh"
 
 namespace flash_prologue {
+
+// Launches fn<<<grid, block, smem, stream>>>(args...) through cudaLaunchKernel
+// and returns the error of this launch only (a launch with <<<>>> reports
+// through cudaGetLastError, which would also return -- and clear -- an error
+// left pending by unrelated earlier work).
+template <typename... P, typename... A>
+inline cudaError_t launch_kernel(void (*fn)(P...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t stream, A&&... args) {
+  static_assert(sizeof...(P) == sizeof...(A), "kernel argument count");
+  std::tuple<std::decay_t<P>...> vals(std::forward<A>(args)...);
+  return std::apply(
+      [&](auto&... v) {
+        void* ptrs[] = {static_cast<void*>(&v)..., nullptr};
+        return cudaLaunchKernel(reinterpret_cast<const void*>(fn), grid, block, ptrs, smem, stream);
+      },
+      vals);
+}
 
 // Index 0 = Q, 1 = K in every two-element array below.
 struct FwdArgs {

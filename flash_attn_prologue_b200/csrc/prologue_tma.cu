@@ -281,6 +281,7 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
   float* dw_s = ds_s + 4 * a.H;                        // [8][D]
   float* iw_s = dw_s + 8 * D;                          // INV: [2 * D] 1 / w
   float* ie_s = iw_s + 2 * D;                          // INV: [H] 1 / exp(scales)
+  __shared__ int wait_failed;  // a consumer warp gave up on a barrier wait
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       mbar_init(&empty[s], kTmaConsumerWarps);
     }
     fence_mbar_init();
+    wait_failed = 0;
   }
   for (int i = threadIdx.x; i < 2 * D; i += kTmaBwdThreads) w_s[i] = a.w[i];
   for (int i = threadIdx.x; i < a.H; i += kTmaBwdThreads) e_s[i] = (float)exp((double)a.scales[i]);
@@ -365,7 +367,10 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       rv0 = load_saved_r(a, tc, t, slot);
       if (S_::PASSES > 1) rv1 = load_saved_r(a, tc, t, S_::ROWS_PER_PASS + slot);
     }
-    if (!mbar_wait(&full[s], (k / S) & 1)) break;
+    if (!mbar_wait(&full[s], (k / S) & 1)) {
+      wait_failed = 1;
+      break;
+    }
     const unsigned char* st = smem + s * stage_bytes;
     const unsigned char* tile_x = st + (2 * t) * kTmaTileBytes;
     const unsigned char* tile_g = st + (2 * t + 1) * kTmaTileBytes;
@@ -460,6 +465,10 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
     }
   }
   consumer_sync(kTmaConsumerWarps * 32);
+  // A CTA whose pipeline timed out has skipped tiles: its partial row is
+  // written as NaN, so the parameter gradients the finalize kernel sums come
+  // out NaN (besides the device error word) instead of silently short.
+  const bool skipped = wait_failed != 0;
   const int C = 2 * D + a.H;
   float* out = a.partials + (int64_t)blockIdx.x * C;
   for (int col = threadIdx.x; col < C; col += kTmaConsumerWarps * 32) {
@@ -474,7 +483,7 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
 #pragma unroll
       for (int w8 = 0; w8 < 4; ++w8) v = __fadd_rn(v, ds_s[w8 * a.H + (col - 2 * D)]);
     }
-    out[col] = v;
+    out[col] = skipped ? __int_as_float(0x7fc00000) : v;
   }
 }
 
@@ -502,8 +511,7 @@ __global__ void __launch_bounds__(32) selftest_wait_timeout_kernel(uint32_t trie
 }
 
 cudaError_t launch_selftest_wait_timeout(uint32_t tries, cudaStream_t stream) {
-  selftest_wait_timeout_kernel<<<1, 32, 0, stream>>>(tries);
-  return cudaGetLastError();
+  return launch_kernel(selftest_wait_timeout_kernel, dim3(1), dim3(32), 0, stream, tries);
 }
 
 // ---------------------------------------------------------------------------

@@ -38,6 +38,7 @@
 
 #include "../../include/flash_prologue.h"
 #include "prologue_common.cuh"
+#include "prologue_host.h"
 #include "tensor_map.h"
 #include "umma_util.cuh"
 
@@ -128,6 +129,7 @@ struct GemmSmem {
   uint64_t* acc_full;      // [2]
   uint64_t* acc_empty;     // [2]
   uint32_t* tmem_slot;
+  uint64_t* drain;         // failure path: completion of every MMA issued (see the MMA issuers)
   float* w_s;              // [2 * D]
 };
 
@@ -142,6 +144,7 @@ __device__ __forceinline__ GemmSmem carve_smem(unsigned char* smem_raw) {
   s.acc_full = s.empty + STAGES;
   s.acc_empty = s.acc_full + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + 2);
+  s.drain = reinterpret_cast<uint64_t*>(s.tmem_slot + 2);  // 8-byte aligned: acc_empty is
   s.w_s = reinterpret_cast<float*>(s.tmem_slot + 4);
   return s;
 }
@@ -406,6 +409,7 @@ __global__ void __launch_bounds__(RolesSingle::kThreads, 1)
       mbar_init(&sm.acc_full[b], 1);
       mbar_init(&sm.acc_empty[b], R::kEpi);
     }
+    mbar_init(sm.drain, 1);
     fence_mbar_init();
   }
   if (warp == R::kMma) {
@@ -473,6 +477,12 @@ __global__ void __launch_bounds__(RolesSingle::kThreads, 1)
         const uint32_t last = tcount - 1;
         mbar_wait(&sm.acc_full[last & 1], (last >> 1) & 1);
       }
+      // A timed-out wait skipped that: wait (bounded) for every MMA issued so
+      // far through one more commit, so TMEM is not released under them.
+      if (failed && it > 0) {
+        umma_commit(sm.drain);
+        mbar_wait(sm.drain, 0);
+      }
     }
   } else {
     run_epilogue<D, kRowsSingle, kStagingBufsSingle, R::kEpi, D / 32>(om, a, sm, tmem_base, blockIdx.x, gridDim.x, 0, 0u);
@@ -514,6 +524,7 @@ __global__ void __launch_bounds__(Roles<EPI>::kThreads, 1)
       mbar_init(&sm.acc_full[b], 1);
       mbar_init(&sm.acc_empty[b], 2 * R::kEpi);  // even CTA: the epilogue warps of both CTAs
     }
+    mbar_init(sm.drain, 1);
     fence_mbar_init();
   }
   if (warp == R::kMma) {
@@ -597,6 +608,12 @@ __global__ void __launch_bounds__(Roles<EPI>::kThreads, 1)
         const uint32_t last = tcount - 1;
         mbar_wait(&sm.acc_full[last & 1], (last >> 1) & 1);
       }
+      // A timed-out wait skipped that: wait (bounded) for every MMA issued so
+      // far through one more commit, so TMEM is not released under them.
+      if (failed && it > 0) {
+        umma_commit_pair(mapa_shared(smem_u32(sm.drain), 0));
+        mbar_wait(sm.drain, 0);
+      }
     }
   } else {
     run_epilogue<D, kRowsPair, kStagingBufsPair, R::kEpi, C::kSlots>(om, a, sm, tmem_base, pair, n_pairs, (int)rank * 128,
@@ -646,8 +663,8 @@ cudaError_t launch_single(const CUtensorMap& mx, const CUtensorMap& mw, const Ou
   const int sms = sm_count();
   if (sms <= 0) return cudaErrorInvalidDevice;
   const int64_t grid = args.n_tiles < sms ? args.n_tiles : sms;
-  qkv_gemm_prologue_kernel<D><<<(unsigned)grid, RolesSingle::kThreads, smem, stream>>>(mx, mw, om, args);
-  return cudaGetLastError();
+  return launch_kernel(qkv_gemm_prologue_kernel<D>, dim3((unsigned)grid), dim3(RolesSingle::kThreads), smem,
+                       stream, mx, mw, om, args);
 }
 
 // Co-resident 2-CTA clusters of a pair kernel on this device (cached).

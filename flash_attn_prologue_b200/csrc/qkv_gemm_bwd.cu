@@ -83,6 +83,7 @@ struct BwdSmem {
   uint64_t* acc_full;      // [2]
   uint64_t* acc_empty;     // [2]
   uint32_t* tmem_slot;
+  uint64_t* drain;         // failure path: completion of every MMA issued
 };
 
 __device__ __forceinline__ BwdSmem carve(unsigned char* raw) {
@@ -94,6 +95,7 @@ __device__ __forceinline__ BwdSmem carve(unsigned char* raw) {
   s.acc_full = s.empty + kStages;
   s.acc_empty = s.acc_full + 2;
   s.tmem_slot = reinterpret_cast<uint32_t*>(s.acc_empty + 2);
+  s.drain = s.acc_empty + 3;  // after the TMEM address slot (16 bytes reserved per 256-byte tail)
   return s;
 }
 constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + kEpiWarps * kStagingPerWarp + 256;
@@ -154,6 +156,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&sm.acc_full[b], 1);
       mbar_init(&sm.acc_empty[b], 2 * kEpiWarps);  // even CTA: the epilogue warps of both CTAs
     }
+    mbar_init(sm.drain, 1);
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
@@ -260,6 +263,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (tcount > 0 && !failed) {
         const uint32_t last = tcount - 1;
         mbar_wait(&sm.acc_full[last & 1], (last >> 1) & 1);
+      }
+      // A timed-out wait skipped that: wait (bounded) for every MMA issued so
+      // far through one more commit, so TMEM is not released under them.
+      if (failed && it > 0) {
+        umma_commit_pair(mapa_shared(smem_u32(sm.drain), 0));
+        mbar_wait(sm.drain, 0);
       }
     }
   } else {
@@ -642,9 +651,11 @@ FLASH_PROLOGUE_API int flash_prologue_qkv_bwd_dw(
   const int sms = device_sms();
   const int64_t blocks = (count / 4 + 255) / 256;
   const int grid = (int)(blocks < 4LL * sms ? blocks : 4LL * sms);
-  qkv_bwd_dw_finalize_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(workspace), a.split, count,
-                                                  static_cast<__nv_bfloat16*>(grad_w), accumulate ? 1 : 0);
-  return cudaGetLastError() == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
+  return launch_kernel(qkv_bwd_dw_finalize_kernel, dim3(grid), dim3(256), 0, s,
+                       static_cast<const float*>(workspace), a.split, count,
+                       static_cast<__nv_bfloat16*>(grad_w), accumulate ? 1 : 0) == cudaSuccess
+             ? FLASH_PROLOGUE_OK
+             : FLASH_PROLOGUE_ERR_CUDA;
 }
 
 }  // extern "C"
