@@ -13,6 +13,38 @@ import torch
 from torch import Tensor, nn
 
 
+_MASTERS = ("rmsnorm_weight", "scales")
+
+
+def _keep_fp32_dtype(fn):
+    """Wraps a Module._apply conversion so that it never changes a tensor's dtype.
+
+    The conversion is first tried on an empty tensor of the same dtype and
+    device. If that keeps the dtype (a device move, ``share_memory_``,
+    ``to_empty``), the conversion itself runs. If it changes the dtype
+    (``.bfloat16()``, ``.half()``, ``.to(dtype)``, with or without a device
+    move), the tensor goes to the probe's device and stays FP32, so its values
+    are never rounded through the narrower type.
+    """
+    def convert(t):
+        probe = fn(t.new_empty(0))
+        if probe.dtype == t.dtype:
+            return fn(t)
+        if t.is_meta:
+            return fn(t).float()
+        return t.to(device=probe.device, dtype=torch.float32)
+    return convert
+
+
+def _masters_back_to_fp32(module, incompatible_keys):
+    """load_state_dict(..., assign=True) installs the checkpoint's own tensors;
+    a lower-precision one is widened back to an FP32 parameter (exactly)."""
+    for name in _MASTERS:
+        p = module._parameters.get(name)
+        if p is not None and p.dtype != torch.float32:
+            module._parameters[name] = nn.Parameter(p.detach().float(), requires_grad=p.requires_grad)
+
+
 class RMSNormRoPEScale(nn.Module):
     """Packed/dense prologue with FP32 master affine and log-scale parameters.
 
@@ -39,25 +71,10 @@ class RMSNormRoPEScale(nn.Module):
         self.rmsnorm_weight = nn.Parameter(torch.empty(2, 1, head_dim, dtype=torch.float32))
         self.scales = nn.Parameter(torch.empty(num_heads, 1, 1, dtype=torch.float32))
         self.reset_parameters()
+        self.register_load_state_dict_post_hook(_masters_back_to_fp32)
 
     def _apply(self, fn, recurse=True):
-        # Device moves follow `fn`; dtype casts do not reach the FP32 masters.
-        def keep_fp32(tensor):
-            target = fn(tensor)
-            if tensor.is_meta or target.is_meta:
-                return target.float()
-            return tensor.to(device=target.device, dtype=torch.float32)
-        return super()._apply(keep_fp32, recurse=recurse)
-
-    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict,
-                              missing_keys, unexpected_keys, error_msgs):
-        # assign=True would otherwise install a lower-precision checkpoint tensor.
-        for name in ("rmsnorm_weight", "scales"):
-            key = prefix + name
-            if key in state_dict:
-                state_dict[key] = state_dict[key].float()
-        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict,
-                                      missing_keys, unexpected_keys, error_msgs)
+        return super()._apply(_keep_fp32_dtype(fn), recurse=recurse)
 
     def bfloat(self):
         """Alias of ``bfloat16()``; the FP32 masters stay FP32."""
