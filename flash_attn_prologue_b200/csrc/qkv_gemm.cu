@@ -249,11 +249,13 @@ __device__ __forceinline__ void run_epilogue(const OutMaps& om, const GemmArgs& 
     const int64_t n0 = (tile % a.n_tiles_n) * BN;
     const int seg = (int)(n0 / (a.H * D));  // the whole tile is Q (0), K (1) or V (2)
     const bool prologue = a.apply_prologue && seg < 2;
+    float e_first = 1.f;  // exp(scale) of this warp's first head of the tile (Q tiles)
     if (prologue) {
       srow = a.sin + b * a.sin_b + sp * a.sin_n;
       crow = a.cos + b * a.cos_b + sp * a.cos_n;
 #pragma unroll
       for (int g = 0; g < SLOTS; ++g) load_group(g, g);
+      if (seg == 0) e_first = (float)exp((double)a.scales[((n0 + head0 * D) % (a.H * D)) / D]);
     }
     if (!mbar_wait(&sm.acc_full[abuf], (tcount >> 1) & 1)) break;
     tc_fence_after();
@@ -287,89 +289,96 @@ __device__ __forceinline__ void run_epilogue(const OutMaps& om, const GemmArgs& 
 #pragma unroll
         for (int g = 0; g < SLOTS; ++g) load_group(g, g);
       }
-      // Pass 1: BF16 projection, optional raw store, sum of squares; 32
-      // columns per step, the next step's TMEM loads in flight meanwhile.
+      const float e = (seg == 0) ? (hh == head0 ? e_first : (float)exp((double)a.scales[h])) : 1.f;
+      float sumsq;
+      // Pass 1: BF16 projection (kept packed in registers for pass 2),
+      // optional raw store, sum of squares; 32 columns per step, the next
+      // step's TMEM loads in flight meanwhile.
       const bool want_raw = a.raw[seg] != nullptr;
       __nv_bfloat16* raw = want_raw ? static_cast<__nv_bfloat16*>(a.raw[seg]) + out_off : nullptr;
-      float2 acc = make_float2(0.f, 0.f);
-      uint32_t va[2][16], vb[2][16];
-      tmem_ld16(tcol, va[0]);
-      tmem_ld16(tcol + 16, vb[0]);
-      tmem_wait_ld_regs(va[0], vb[0]);
+      uint32_t px[D / 2];  // px[i] = BF16 columns 2i, 2i + 1 of the head
+      {
+        float2 acc = make_float2(0.f, 0.f);
+        uint32_t va[16], vb[16];  // one TMEM buffer: step c + 1 loads while step c's packed values are used
+        tmem_ld16(tcol, va);
+        tmem_ld16(tcol + 16, vb);
+        tmem_wait_ld_regs(va, vb);
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        const int nb = (c + 1) & 1;
-        if (c + 1 < D / 32) {
-          tmem_ld16(tcol + 32 * (c + 1), va[nb]);
-          tmem_ld16(tcol + 32 * (c + 1) + 16, vb[nb]);
-        }
-        uint32_t p[16];
+        for (int c = 0; c < D / 32; ++c) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          p[i] = pack_bf16(make_float2(__uint_as_float(va[c & 1][2 * i]), __uint_as_float(va[c & 1][2 * i + 1])));
-          p[8 + i] = pack_bf16(make_float2(__uint_as_float(vb[c & 1][2 * i]), __uint_as_float(vb[c & 1][2 * i + 1])));
-        }
+          for (int i = 0; i < 8; ++i) {
+            px[16 * c + i] = pack_bf16(make_float2(__uint_as_float(va[2 * i]), __uint_as_float(va[2 * i + 1])));
+            px[16 * c + 8 + i] = pack_bf16(make_float2(__uint_as_float(vb[2 * i]), __uint_as_float(vb[2 * i + 1])));
+          }
+          if (c + 1 < D / 32) {
+            tmem_ld16(tcol + 32 * (c + 1), va);
+            tmem_ld16(tcol + 32 * (c + 1) + 16, vb);
+          }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 x = unpack_bf16(p[i]);
-          acc = __ffma2_rn(x, x, acc);  // squares of BF16 values are exact in FP32
-        }
-        if (want_raw) {
+          for (int i = 0; i < 16; ++i) {
+            const float2 x = unpack_bf16(px[16 * c + i]);
+            acc = __ffma2_rn(x, x, acc);  // squares of BF16 values are exact in FP32
+          }
+          if (want_raw) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            emit16(raw, valid, 32 * c + 8 * q, make_uint4(p[4 * q], p[4 * q + 1], p[4 * q + 2], p[4 * q + 3]));
+            for (int q = 0; q < 4; ++q)
+              emit16(raw, valid, 32 * c + 8 * q,
+                     make_uint4(px[16 * c + 4 * q], px[16 * c + 4 * q + 1], px[16 * c + 4 * q + 2], px[16 * c + 4 * q + 3]));
+          }
+          if (c + 1 < D / 32) tmem_wait_ld_regs(va, vb);
         }
-        if (c + 1 < D / 32) tmem_wait_ld_regs(va[nb], vb[nb]);
+        sumsq = __fadd_rn(acc.x, acc.y);
       }
-      // Pass 2's first group is requested before the raw store's wait.
-      tmem_ld16(tcol, va[0]);
-      tmem_ld16(tcol + HALF, vb[0]);
       if (want_raw && staged) {
         flush(&om.m[3 + seg], row0);
         reclaim();
       }
-      tmem_wait_ld_regs(va[0], vb[0]);
-      const float r = inv_rms<D>(__fadd_rn(acc.x, acc.y), a.eps);
+      const float r = inv_rms<D>(sumsq, a.eps);
       const float2 r2 = splat2(r);
-      const float2 e2 = splat2(seg == 0 ? (float)exp((double)a.scales[h]) : 1.f);
+      const float2 e2 = splat2(e);
       const float* wrow = sm.w_s + seg * D;
-      // Pass 2, 16 columns at a time: columns j and j + D/2 of the head are
-      // in this thread; each product and sum rounds like the eager formulation.
+      // Pass 2, 16 columns at a time from the registers of pass 1: columns j
+      // and j + D/2 of the head are in this thread; each product and sum
+      // rounds like the eager formulation.
 #pragma unroll
       for (int g = 0; g < GROUPS; ++g) {
         const int slot = g % SLOTS;
-        const int gb = g & 1, nb = (g + 1) & 1;
-        if (g + 1 < GROUPS) {
-          tmem_ld16(tcol + 16 * (g + 1), va[nb]);
-          tmem_ld16(tcol + HALF + 16 * (g + 1), vb[nb]);
-        }
+        // The group's words are "defined" here for the compiler, so their
+        // unpacking is not hoisted into earlier groups (which would hold every
+        // column of the head unpacked at once and spill).
+#pragma unroll
+        for (int i = 0; i < 8; ++i) asm volatile("" : "+r"(px[8 * g + i]), "+r"(px[HALF / 2 + 8 * g + i]));
         uint32_t p1[8], p2[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 8; i += 2) {
           const int j = 16 * g + 2 * i;  // column pair within the first half
-          const float2 x1 = unpack_bf16(pack_bf16(make_float2(__uint_as_float(va[gb][2 * i]), __uint_as_float(va[gb][2 * i + 1]))));
-          const float2 x2 = unpack_bf16(pack_bf16(make_float2(__uint_as_float(vb[gb][2 * i]), __uint_as_float(vb[gb][2 * i + 1]))));
-          const float2 wa = ld_pair(wrow, j / 2);
-          const float2 wb = ld_pair(wrow + HALF, j / 2);
-          const float2 c2 = make_float2(cs[slot][2 * i], cs[slot][2 * i + 1]);
-          const float2 s2 = make_float2(sn[slot][2 * i], sn[slot][2 * i + 1]);
-          const float2 y1 = __fmul2_rn(__fmul2_rn(x1, r2), wa);
-          const float2 y2 = __fmul2_rn(__fmul2_rn(x2, r2), wb);
-          float2 o1 = __fadd2_rn(__fmul2_rn(y1, c2), neg2(__fmul2_rn(y2, s2)));
-          float2 o2 = __fadd2_rn(__fmul2_rn(y2, c2), __fmul2_rn(y1, s2));
-          if (seg == 0) {
-            o1 = __fmul2_rn(o1, e2);
-            o2 = __fmul2_rn(o2, e2);
+          const float4 wa4 = *reinterpret_cast<const float4*>(wrow + j);
+          const float4 wb4 = *reinterpret_cast<const float4*>(wrow + HALF + j);
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const float2 x1 = unpack_bf16(px[8 * g + i + u]);
+            const float2 x2 = unpack_bf16(px[HALF / 2 + 8 * g + i + u]);
+            const float2 wa = u ? make_float2(wa4.z, wa4.w) : make_float2(wa4.x, wa4.y);
+            const float2 wb = u ? make_float2(wb4.z, wb4.w) : make_float2(wb4.x, wb4.y);
+            const float2 c2 = make_float2(cs[slot][2 * (i + u)], cs[slot][2 * (i + u) + 1]);
+            const float2 s2 = make_float2(sn[slot][2 * (i + u)], sn[slot][2 * (i + u) + 1]);
+            const float2 y1 = __fmul2_rn(__fmul2_rn(x1, r2), wa);
+            const float2 y2 = __fmul2_rn(__fmul2_rn(x2, r2), wb);
+            float2 o1 = __fadd2_rn(__fmul2_rn(y1, c2), neg2(__fmul2_rn(y2, s2)));
+            float2 o2 = __fadd2_rn(__fmul2_rn(y2, c2), __fmul2_rn(y1, s2));
+            if (seg == 0) {
+              o1 = __fmul2_rn(o1, e2);
+              o2 = __fmul2_rn(o2, e2);
+            }
+            p1[i + u] = pack_bf16(o1);
+            p2[i + u] = pack_bf16(o2);
           }
-          p1[i] = pack_bf16(o1);
-          p2[i] = pack_bf16(o2);
         }
         if (GROUPS > SLOTS && g + SLOTS < GROUPS) load_group(g + SLOTS, slot);
         emit16(out, valid, 16 * g, make_uint4(p1[0], p1[1], p1[2], p1[3]));
         emit16(out, valid, 16 * g + 8, make_uint4(p1[4], p1[5], p1[6], p1[7]));
         emit16(out, valid, HALF + 16 * g, make_uint4(p2[0], p2[1], p2[2], p2[3]));
         emit16(out, valid, HALF + 16 * g + 8, make_uint4(p2[4], p2[5], p2[6], p2[7]));
-        if (g + 1 < GROUPS) tmem_wait_ld_regs(va[nb], vb[nb]);
       }
       if (staged) flush(&om.m[seg], row0);
     }
