@@ -50,6 +50,9 @@ BWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 6 + HEAD_DIM * 4
 # kernel ends are not counted by the capture, so traffic reads slightly below
 # the algorithmic bytes.
 NCU_TRAFFIC_BYTES_PER_TOKEN = {"fwd": 8018, "bwd": 12131}
+# sm__pipe_tensor_cycles_active (% of active cycles) of the fused QKV GEMM +
+# prologue kernel in one ncu capture at C5 size (summary kept under profiles/).
+NCU_C5_TENSOR_ACTIVE_PCT = 77.1
 
 
 def measured_peak():
@@ -62,40 +65,70 @@ def measured_peak():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples during the timed region."""
+    """nvidia-smi clock/throttle samples over a marked region (warm-up + timed steps).
+
+    The sampler process starts (and has produced its first sample) before the
+    region begins, a reader thread timestamps every line, and the summary keeps
+    the samples that arrived between ``begin()`` and ``end()``.
+    """
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
+    def __init__(self, index, period_ms=20):
         self.index = index
+        self.period_ms = period_ms
         self.proc = None
+        self.samples = []
+        self.t0 = self.t1 = None
 
     def __enter__(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.period_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return self
+        first = threading.Event()
+
+        def reader():
+            for ln in self.proc.stdout:
+                if ln.strip():
+                    self.samples.append((time.perf_counter(), ln))
+                    first.set()
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        first.wait(timeout=5.0)
         return self
 
+    def begin(self):
+        self.t0 = time.perf_counter()
+
+    def end(self):
+        self.t1 = time.perf_counter()
+
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
+            time.sleep(2 * self.period_ms / 1000.0)  # the sample covering the region's end
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                out = ""
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            self.thread.join(timeout=5)
 
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        t0 = self.t0 if self.t0 is not None else -1e30
+        t1 = (self.t1 if self.t1 is not None else 1e30) + self.period_ms / 1000.0
+        for ts, ln in self.samples:
+            if not (t0 <= ts <= t1):
+                continue
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -107,10 +140,11 @@ class ClockSampler:
             for nm, val in zip(names, parts[5:9]):
                 if val.lower() == "active":
                     reasons.add(nm)
+        window = round((self.t1 - self.t0) * 1e3, 1) if self.t0 is not None and self.t1 is not None else None
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "window_ms": window}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window_ms": window}
 
 
 def rope_tables(positions, d, theta):
@@ -210,9 +244,38 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def min_over_ranks(value, world):
+    return -max_over_ranks(-value, world)
+
+
+def _timed_loop(fn, steps, warmup, world, finish=None):
+    """Barrier + synchronize on both sides of `steps` calls of fn(); device time (ms) per
+    call, max over ranks. fn runs on the current stream (and may fork work off it);
+    finish() joins forked work into the current stream before the end event."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        fn()
+    if finish is not None:
+        finish()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    if finish is not None:
+        finish()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(end), world) / steps
+
+
 def run_ours(args, world, rank, local):
     from flash_attn_prologue_b200 import prepare_backend, qknorm_rope_scale
-    from flash_attn_prologue_b200.distributed import reduce_param_grads
+    from flash_attn_prologue_b200.distributed import ParamGradReducer, reduce_param_grads
     prepare_backend("cute")
     device = torch.device("cuda", torch.cuda.current_device())
     T = args.tokens
@@ -222,7 +285,8 @@ def run_ours(args, world, rank, local):
     s.requires_grad_()
 
     stream = torch.cuda.current_stream()
-    fwd_ev, bwd_ev = [], []
+    reducer = ParamGradReducer(device=device) if world > 1 else None
+    fwd_ev, bwd_ev, coll_ev = [], [], []
 
     def step(record=False):
         qq = q.detach().requires_grad_()
@@ -237,41 +301,74 @@ def run_ours(args, world, rank, local):
             e2 = torch.cuda.Event(enable_timing=True); e2.record(stream)
             fwd_ev.append((e0, e1))
             bwd_ev.append((e1, e2))
-        if world > 1:
-            dw, ds = reduce_param_grads(dw, ds)
+        if reducer is not None:
+            # The parameter-gradient reduction on a side stream, overlapping the
+            # next step's forward; its events time it on that stream.
+            if record:
+                c0 = torch.cuda.Event(enable_timing=True)
+                c1 = torch.cuda.Event(enable_timing=True)
+                reducer.stream.wait_stream(stream)
+                c0.record(reducer.stream)
+            dw, ds = reducer.reduce(dw, ds)
+            if record:
+                c1.record(reducer.stream)
+                coll_ev.append((c0, c1))
         return out, dq, dk, dw, ds
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        clocks.begin()
+        for _ in range(args.warmup):
+            step()
+        if reducer is not None:
+            reducer.wait()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):
             step(record=True)
+        if reducer is not None:
+            reducer.wait()  # the last reduction is part of the timed work
         end.record(stream)
         torch.cuda.synchronize()
+        clocks.end()
     barrier(world)
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
     fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_ev)
     bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in bwd_ev)
+    fwd_ms, bwd_ms = max_over_ranks(fwd_ms, world), max_over_ranks(bwd_ms, world)
 
     ms_per_step = elapsed_ms / args.steps
     step_bytes = T * (FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN)
     value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
     mtok = world * T / (ms_per_step * 1e-3) / 1e6
+    peak, peak_kind = measured_peak()
+
+    coll = None
+    if world > 1:
+        # The reduction alone: on its side stream inside the step (from the end of
+        # the backward to the sum's completion, so it includes waiting for the
+        # slowest rank), and isolated (back-to-back on the main stream).
+        side = [a.elapsed_time(b) for a, b in coll_ev]
+        dw0 = torch.randn(2, 1, HEAD_DIM, device=device)
+        ds0 = torch.randn(HEADS, 1, 1, device=device)
+        iso = _timed_loop(lambda: reduce_param_grads(dw0, ds0), 50, 5, world)
+        coll = {"in_step_ms": round(max_over_ranks(statistics.mean(side), world), 4),
+                "in_step_max_ms": round(max_over_ranks(max(side), world), 4),
+                "isolated_ms": round(iso, 4), "floats": 2 * HEAD_DIM + HEADS,
+                "how": "pack + NCCL all_gather + column sum, side stream"}
+    del buf, gq, gk
+
+    c4 = run_c4(args, device, world, rank, peak)
+    c3 = run_c3(args, device, world, rank, peak)
 
     # ---- end to end: host buffers through the public API, copies timed ----
-    e2e = run_e2e(args, T, device, w, s, world)
+    e2e = run_e2e(args, T, device, w, s, world, local)
 
-    peak, peak_kind = measured_peak()
-    bwd_bytes = T * BWD_BYTES_PER_TOKEN
-    fwd_bytes = T * FWD_BYTES_PER_TOKEN
-    bwd_gbs = bwd_bytes / (bwd_ms * 1e-3) / 1e9
-    fwd_gbs = fwd_bytes / (fwd_ms * 1e-3) / 1e9
+    bwd_gbs = T * BWD_BYTES_PER_TOKEN / (bwd_ms * 1e-3) / 1e9
+    fwd_gbs = T * FWD_BYTES_PER_TOKEN / (fwd_ms * 1e-3) / 1e9
     traffic = NCU_TRAFFIC_BYTES_PER_TOKEN["bwd"]
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -279,22 +376,18 @@ def run_ours(args, world, rank, local):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": f"C2 packed fwd+bwd, T={T} tokens per GPU, H={HEADS}, D={HEAD_DIM}, "
-                               "q/k strided views of a [T,3,H,D] BF16 QKV buffer, sin/cos FP32 [T,32]",
-                   "tokens_per_gpu": T, "heads": HEADS, "head_dim": HEAD_DIM,
-                   "l2": "inputs larger than L2 (6.4 GB buffer per GPU), no flush",
-                   "parallelism": f"dp{world}"},
+                               "q/k strided views of a [T,3,H,D] BF16 buffer",
+                   "l2": "inputs > L2 (6.4 GB per GPU), no flush", "parallelism": f"dp{world}"},
         "mtokens_per_s": round(mtok, 3),
         "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 2),
-        "fwd": {"ms": round(fwd_ms, 4), "gbs": round(fwd_gbs, 1),
-                "frac_of_measured": round(fwd_gbs / peak, 4),
-                "pct_of_8tbs": round(100 * fwd_gbs / NOMINAL_HBM_GBS, 2)},
-        "bwd": {"ms": round(bwd_ms, 4), "gbs": round(bwd_gbs, 1),
-                "frac_of_measured": round(bwd_gbs / peak, 4),
-                "pct_of_8tbs": round(100 * bwd_gbs / NOMINAL_HBM_GBS, 2)},
-        "roofline": {"kernel": "prologue_bwd_tma_kernel (+ finalize)", "bound": "hbm",
+        "fwd": {"ms": round(fwd_ms, 4), "gbs": round(fwd_gbs, 1), "frac": round(fwd_gbs / peak, 4)},
+        "bwd": {"ms": round(bwd_ms, 4), "gbs": round(bwd_gbs, 1), "frac": round(bwd_gbs / peak, 4)},
+        "roofline": {"kernel": "prologue_bwd_tma_kernel+finalize", "bound": "hbm",
                      "achieved": round(bwd_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(bwd_gbs / peak, 4), "peak_source": peak_kind,
-                     "traffic": (round(traffic * T) if traffic else None)},
+                     "traffic": (round(traffic * T) if traffic else None),
+                     "traffic_src": "ncu at T=131072, x8 to T"},
+        "collective": coll, "c3": c3, "c4": c4,
         "e2e": e2e,
         "gpu_launches": 3 * args.steps,
         "clocks": clocks.summary(),
@@ -307,9 +400,72 @@ def run_ours(args, world, rank, local):
                                 "sample": f"{args.cpu_tokens} tokens of C2 fwd+bwd, median of "
                                           f"{args.cpu_reps}, torch eager CPU port of native"}
     if rank == 0 and world == 1 and not args.no_extras:
-        line["other_configs"] = run_extras(device)
+        line["x"] = run_extras(device, peak)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line, separators=(",", ":")), flush=True)
+    if args.detail and rank == 0:
+        Path(args.detail).write_text(json.dumps(line, indent=1))
+
+
+def run_c4(args, device, world, rank, peak):
+    """C4: packed backward of T=262,144 tokens (H=8, D=64) per rank, then the
+    reduction of d rmsnorm_weight / d scales over the ranks (weak scaling)."""
+    from flash_attn_prologue_b200.distributed import ParamGradReducer
+    T, H, D = 262144, 8, 64
+    g = torch.Generator(device=device).manual_seed(40 + rank)
+    q, k, gq, gk = (torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16)
+                    for _ in range(4))
+    sin, cos = rope_tables(torch.arange(T, device=device), D, 10000.0)
+    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
+    s = 0.1 * torch.randn(H, 1, 1, generator=g, device=device)
+    bwd = torch.ops.flash_prologue.qknorm_rope_scale_cute_backward
+    q4, k4 = q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None]
+    g4q, g4k = gq.permute(1, 0, 2)[None], gk.permute(1, 0, 2)[None]
+    s4 = sin[None, None].expand(1, 1, T, D // 2)
+    c4 = cos[None, None].expand(1, 1, T, D // 2)
+    reducer = ParamGradReducer(device=device) if world > 1 else None
+
+    def step():
+        dq, dk, dw, ds = bwd(q4, k4, w, s, s4, c4, g4q, g4k, 1e-5)
+        if reducer is not None:
+            reducer.reduce(dw, ds)
+
+    def join():
+        if reducer is not None:
+            reducer.wait()
+
+    def step_serial():
+        step()
+        join()
+
+    # Each step's reduction overlaps the next step's backward (the last one is
+    # joined inside the timing); "ms_serial" waits for every reduction in turn.
+    ms = _timed_loop(step, args.steps, args.warmup, world, finish=join)
+    ms_serial = _timed_loop(step_serial, args.steps, args.warmup, world)
+    nbytes = T * (H * D * 2 * 6 + D * 4)
+    gbs = world * nbytes / (ms * 1e-3) / 1e9
+    return {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac": round(gbs / world / peak, 4),
+            "ms_serial": round(ms_serial, 4), "tokens_per_gpu": T, "scaling": "weak"}
+
+
+def run_c3(args, device, world, rank, peak):
+    """C3: dense forward [B=8, H=32, S=8192, D=128], the batch sharded over the
+    ranks (strong scaling: the whole problem's bytes over the slowest rank's time)."""
+    from flash_attn_prologue_b200 import qknorm_rope_scale
+    from flash_attn_prologue_b200.distributed import shard_range
+    B, H, S, D = 8, 32, 8192, 128
+    b0, b1 = shard_range(B, rank, world)
+    g = torch.Generator(device=device).manual_seed(30 + rank)
+    q, k = (torch.randn(b1 - b0, H, S, D, generator=g, device=device).to(torch.bfloat16) for _ in range(2))
+    sin, cos = rope_tables(torch.arange(S, device=device), D, 500000.0)
+    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
+    s = torch.full((H, 1, 1), math.log(1 / math.sqrt(D)), device=device)
+    ms = _timed_loop(lambda: qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute"),
+                     args.steps, args.warmup, world)
+    nbytes = B * H * S * D * 2 * 4 + S * D * 4
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac": round(gbs / world / peak, 4),
+            "batches_per_gpu": b1 - b0, "scaling": "strong"}
 
 
 def _event_ms(fn, steps, warmup=3):
@@ -327,25 +483,32 @@ def _event_ms(fn, steps, warmup=3):
     return start.elapsed_time(end) / steps
 
 
-def run_extras(device, steps=20):
-    """The other benchmark configurations, timed on one GPU (reported beside the headline).
+def run_extras(device, peak, steps=20):
+    """The other single-GPU measurements, compact (reported beside the headline at N = 1).
 
-    C1 packed fwd [4096, 4, 32] (launch-latency bound); C3 dense fwd
-    [8, 32, 8192, 128]; C4 packed bwd [262144, 8, 64]; C5 fused QKV GEMM +
-    prologue, X [65536, 2048] x W [6144, 2048] (H=16, D=128), beside the same
-    work as cuBLAS F.linear followed by this library's prologue kernel.
+    c1: C1 packed fwd [4096, 4, 32] eager and as one CUDA-graph replay.
+    inv: C2 through the inverse formulation (fwd also stores r; bwd rebuilds rows).
+    qkv_step: C2 training step to the [T, 3, H, D] gradient, through slice views
+      + autograd gather, and through qknorm_rope_scale_qkv.
+    c5: fused QKV GEMM + prologue, X [65536, 2048] x W [6144, 2048] (H=16, D=128):
+      burst (`steps` launches) and sustained (450 launches, power-capped clocks)
+      times of the fused kernel, the same kernel without the prologue, cuBLAS
+      F.linear alone and F.linear + this prologue kernel; fractions against the
+      measured bf16_tflops (burst) and bf16_tflops_sustained.
+    c5_bwd: projection backward dX / dW kernels (gradients read in place), cuBLAS on
+      an already gathered [T, 3HD] dP, and that gather.
+    c5_step: forward + backward to x, W, rmsnorm_weight, scales: fused op vs
+      F.linear + qknorm_rope_scale + autograd (cuBLAS).
     """
     import flash_attn_prologue_b200 as fap
     from flash_attn_prologue_b200 import qknorm_rope_scale
     out = {}
     g = torch.Generator(device=device).manual_seed(5)
-    peak, _ = measured_peak()
     bf16_peak = _measured("bf16_tflops", 1590.0)
+    r4 = lambda v: round(v, 4)  # noqa: E731
 
-    def hbm(name, nbytes, ms):
-        gbs = nbytes / (ms * 1e-3) / 1e9
-        out[name] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4),
-                     "pct_of_8tbs": round(100 * gbs / NOMINAL_HBM_GBS, 2), "algorithmic_bytes": nbytes}
+    def frac(nbytes, ms):
+        return r4(nbytes / (ms * 1e-3) / 1e9 / peak)
 
     # C1
     T, H, D = 4096, 4, 32
@@ -353,41 +516,14 @@ def run_extras(device, steps=20):
     sin, cos = rope_tables(torch.arange(T, device=device), D, 10000.0)
     w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
     s = torch.zeros(H, 1, 1, device=device)
-    c1_bytes = T * (H * D * 2 * 4 + D * 4)
-    hbm("c1_fwd", c1_bytes, _event_ms(lambda: qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute"), steps))
-    # The same call captured once into a CUDA graph and replayed: the kernel
-    # without the Python / dispatch overhead of each eager call.
+    eager = _event_ms(lambda: qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute"), steps)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute")
-    hbm("c1_fwd_graph_replay", c1_bytes, _event_ms(graph.replay, max(steps, 200)))
-    # C3
-    B, H, S, D = 8, 32, 8192, 128
-    q, k = (torch.randn(B, H, S, D, generator=g, device=device).to(torch.bfloat16) for _ in range(2))
-    sin, cos = rope_tables(torch.arange(S, device=device), D, 500000.0)
-    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
-    s = torch.full((H, 1, 1), math.log(1 / math.sqrt(D)), device=device)
-    hbm("c3_fwd", B * H * S * D * 2 * 4 + S * D * 4,
-        _event_ms(lambda: qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute"), steps))
-    del q, k
-    # C4 (one rank's backward; the NCCL reduction is part of the multi-GPU step)
-    T, H, D = 262144, 8, 64
-    q, k, gq, gk = (torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16)
-                    for _ in range(4))
-    sin, cos = rope_tables(torch.arange(T, device=device), D, 10000.0)
-    w = 1 + 0.02 * torch.randn(2, 1, D, generator=g, device=device)
-    s = 0.1 * torch.randn(H, 1, 1, generator=g, device=device)
-    bwd = torch.ops.flash_prologue.qknorm_rope_scale_cute_backward
-    q4, k4 = q.permute(1, 0, 2)[None], k.permute(1, 0, 2)[None]
-    g4q, g4k = gq.permute(1, 0, 2)[None], gk.permute(1, 0, 2)[None]
-    s4 = sin[None, None].expand(1, 1, T, D // 2)
-    c4 = cos[None, None].expand(1, 1, T, D // 2)
-    hbm("c4_bwd", T * (H * D * 2 * 6 + D * 4),
-        _event_ms(lambda: bwd(q4, k4, w, s, s4, c4, g4q, g4k, 1e-5), steps))
-    del q, k, gq, gk
-    # C2 through the inverse formulation (forward also stores r per row; the
-    # backward rebuilds rows from the outputs and r): strided views of the
-    # [T, 3, H, D] buffer, algorithmic bytes + 4 B per row of r.
+    out["c1"] = {"ms": r4(eager), "graph_ms": r4(_event_ms(graph.replay, max(steps, 200)))}
+    del graph
+    # C2 through the inverse formulation: strided views of the [T, 3, H, D]
+    # buffer, algorithmic bytes + 4 B per row of r.
     T, H, D = T_TOKENS, HEADS, HEAD_DIM
     buf = torch.randn(T, 3, H, D, generator=g, device=device).to(torch.bfloat16)
     q4, k4 = (buf[:, i].permute(1, 0, 2)[None] for i in (0, 1))
@@ -400,34 +536,29 @@ def run_extras(device, steps=20):
     inv_fwd = torch.ops.flash_prologue.qknorm_rope_scale_cute_inverse
     inv_bwd = torch.ops.flash_prologue.qknorm_rope_scale_cute_inverse_backward
     qo, ko, rq, rk = inv_fwd(q4, k4, w, s, s4, c4, 1e-5)
-    hbm("c2_inverse_fwd", T * (H * D * 2 * 4 + D * 4 + 2 * H * 4),
-        _event_ms(lambda: inv_fwd(q4, k4, w, s, s4, c4, 1e-5), steps))
-    hbm("c2_inverse_bwd", T * (H * D * 2 * 6 + D * 4 + 2 * H * 4),
-        _event_ms(lambda: inv_bwd(qo, ko, w, s, s4, c4, g4q, g4k, rq, rk, 1e-5), steps))
+    f_ms = _event_ms(lambda: inv_fwd(q4, k4, w, s, s4, c4, 1e-5), steps)
+    b_ms = _event_ms(lambda: inv_bwd(qo, ko, w, s, s4, c4, g4q, g4k, rq, rk, 1e-5), steps)
+    out["inv"] = {"fwd_ms": r4(f_ms), "fwd_frac": frac(T * (FWD_BYTES_PER_TOKEN + 2 * H * 4), f_ms),
+                  "bwd_ms": r4(b_ms), "bwd_frac": frac(T * (BWD_BYTES_PER_TOKEN + 2 * H * 4), b_ms)}
     del q4, k4, qo, ko, rq, rk
-    # C2 training step with the QKV gradient: forward + autograd backward to the
-    # [T, 3, H, D] buffer, V's gradient included. Through slice views
-    # (q, k, v = qkv.unbind(1) + qknorm_rope_scale: autograd gathers dq, dk, dv
-    # into the buffer's gradient) and through qknorm_rope_scale_qkv (the kernel
-    # writes dq, dk into the gradient buffer's slots; dv is copied into its slot).
+    # C2 training step with the QKV gradient (V's gradient included).
     gq3, gk3 = (t[0].permute(1, 0, 2) for t in (g4q, g4k))
     gv3 = torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16)
-    s2, c2 = sin, cos
 
     def step_slices():
         x = buf.detach().requires_grad_()
         q, k, v = x.unbind(1)
-        qo_, ko_ = qknorm_rope_scale(q, k, w, s, s2, c2, backend="cute")
+        qo_, ko_ = qknorm_rope_scale(q, k, w, s, sin, cos, backend="cute")
         return torch.autograd.grad((qo_, ko_, v), x, (gq3, gk3, gv3))
 
     def step_packed():
         x = buf.detach().requires_grad_()
-        qo_, ko_, v = fap.qknorm_rope_scale_qkv(x, w, s, s2, c2)
+        qo_, ko_, v = fap.qknorm_rope_scale_qkv(x, w, s, sin, cos)
         return torch.autograd.grad((qo_, ko_, v), x, (gq3, gk3, gv3))
 
     step_bytes = T * (FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN + H * D * 2 * 2)  # + dv read/write
-    for name, fn in (("c2_qkv_step_slice_views", step_slices), ("c2_qkv_step_packed_gradient", step_packed)):
-        hbm(name, step_bytes, _event_ms(fn, steps))
+    sl_ms, pk_ms = _event_ms(step_slices, steps), _event_ms(step_packed, steps)
+    out["qkv_step"] = {"slices_ms": r4(sl_ms), "packed_ms": r4(pk_ms), "packed_frac": frac(step_bytes, pk_ms)}
     del buf, g4q, g4k, gq3, gk3, gv3
     # C5
     T, hidden, H, D = 65536, 2048, 16, 128
@@ -438,62 +569,49 @@ def run_extras(device, steps=20):
     s = 0.1 * torch.randn(H, 1, 1, generator=g, device=device)
     flop = 2 * T * 3 * H * D * hidden
 
-    def fused():
-        return fap.fused_qkv_epilogue(x, wq, w, s, sin, cos)
-
-    def gemm_only():
-        return fap.fused_qkv(x, wq)
-
     def unfused():
         p = torch.nn.functional.linear(x[0], wq).view(T, 3, H, D)
         return qknorm_rope_scale(p[:, 0], p[:, 1], w, s, sin, cos, backend="cute")
 
-    def linear():
-        return torch.nn.functional.linear(x[0], wq)
-
-    sustained_sm = _measured("bf16_tflops_sustained", 1410.0)
-    c5 = {"bf16_peak_tflops": bf16_peak, "bf16_sustained_peak_tflops": sustained_sm, "flop": flop}
+    fns = (("fused", lambda: fap.fused_qkv_epilogue(x, wq, w, s, sin, cos)),
+           ("gemm_only", lambda: fap.fused_qkv(x, wq)),
+           ("cublas", lambda: torch.nn.functional.linear(x[0], wq)),
+           ("cublas_prologue", unfused))
+    sustained_peak = _measured("bf16_tflops_sustained", 1410.0)
+    c5 = {}
     # Burst: `steps` launches; sustained: ~0.6 s of back-to-back launches, where
     # the 1 kW power cap sets the clocks (the regime of a long training run).
-    for regime, n in (("burst", steps), ("sustained", 450)):
-        ms = {name: _event_ms(fn, n) for name, fn in
-              (("fused", fused), ("gemm_only", gemm_only), ("cublas_linear_then_prologue_kernel", unfused),
-               ("cublas_linear_alone", linear))}
-        peak_ref = bf16_peak if regime == "burst" else sustained_sm
+    for regime, n, pk in (("", steps, bf16_peak), ("sus_", 450, sustained_peak)):
+        ms = {name: _event_ms(fn, n) for name, fn in fns}
         tf = flop / (ms["fused"] * 1e-3) / 1e12
-        c5[regime] = {"launches": n, "tflops": round(tf, 1), "frac_of_measured_bf16": round(tf / peak_ref, 4),
-                      **{f"{k}_ms": round(v, 4) for k, v in ms.items()}}
-    c5["ms"] = c5["burst"]["fused_ms"]
-    c5["tflops"] = c5["burst"]["tflops"]
-    c5["frac_of_measured_bf16"] = c5["burst"]["frac_of_measured_bf16"]
-    c5["note"] = ("fused = one tcgen05 kernel (2-CTA clusters, cta_group::2) writing Q,K (prologue applied), "
-                  "V and the BF16 Q/K projections; gemm_only = the same kernel without the prologue; "
-                  "burst fractions against bf16_tflops, sustained against bf16_tflops_sustained")
-    out["c5_fused_qkv_gemm"] = c5
+        if not regime:
+            c5["tflops"] = round(tf, 1)
+        c5[f"{regime}frac"] = r4(tf / pk)
+        c5.update({f"{regime}{name}_ms": r4(v) for name, v in ms.items()})
+    c5["ncu_tensor_active_pct"] = NCU_C5_TENSOR_ACTIVE_PCT
+    out["c5"] = c5
     # C5 projection backward: dX = dP W and dW = dP^T X with dP the per-head
-    # [1, H, T, D] gradients, by the hand-written kernels (read in place) and,
-    # for comparison, by cuBLAS on an already gathered [T, 3HD] dP.
+    # [1, H, T, D] gradients, by the hand-written kernels (read in place) and
+    # by cuBLAS on an already gathered [T, 3HD] dP.
     gq5, gk5, gv5 = (torch.randn(1, H, T, D, generator=g, device=device).to(torch.bfloat16) for _ in range(3))
-    dp = torch.stack((gq5, gk5, gv5), 0).permute(1, 3, 0, 2, 4).reshape(T, 3 * H * D).contiguous()
+
+    def gather():
+        return torch.stack((gq5, gk5, gv5), 0).permute(1, 3, 0, 2, 4).reshape(T, 3 * H * D).contiguous()
+
+    dp = gather()
     x2 = x[0]
     ms = {name: _event_ms(fn, steps) for name, fn in (
         ("dx", lambda: fap.matmul_bwd_dx(gq5, gk5, gv5, wq)),
         ("dw", lambda: fap.matmul_bwd_dw(gq5, gk5, gv5, x)),
-        ("cublas_dx_on_gathered_dp", lambda: dp @ wq),
-        ("cublas_dw_on_gathered_dp", lambda: dp.t() @ x2),
-        ("gather_dp", lambda: torch.stack((gq5, gk5, gv5), 0).permute(1, 3, 0, 2, 4).reshape(T, 3 * H * D)
-         .contiguous()))}
-    bwd = {f"{k}_ms": round(v, 4) for k, v in ms.items()}
+        ("cublas_dx", lambda: dp @ wq),
+        ("cublas_dw", lambda: dp.t() @ x2),
+        ("gather", gather))}
+    c5b = {f"{k}_ms": r4(v) for k, v in ms.items()}
     for k in ("dx", "dw"):
-        tf = flop / (ms[k] * 1e-3) / 1e12
-        bwd[f"{k}_tflops"] = round(tf, 1)
-        bwd[f"{k}_frac_of_measured_bf16"] = round(tf / bf16_peak, 4)
-    bwd["note"] = ("dx/dw = tcgen05 GEMM kernels reading the [B, H, N, D] gradients through TMA (no gather); "
-                   "cublas_* = torch matmul on a dP already gathered to [T, 3HD], gather_dp = that gather")
-    out["c5_projection_backward"] = bwd
-    # C5 training step: forward + backward to x, W, rmsnorm_weight and scales
-    # through the fused op, and through the reference's composition
-    # (cuBLAS F.linear, this prologue op, autograd's cuBLAS GEMMs for the linear).
+        c5b[f"{k}_frac"] = r4(flop / (ms[k] * 1e-3) / 1e12 / bf16_peak)
+    out["c5_bwd"] = c5b
+    del dp
+    # C5 training step: forward + backward to x, W, rmsnorm_weight and scales.
     xg = x.detach().requires_grad_()
     wg = wq.detach().requires_grad_()
     wr = w.detach().requires_grad_()
@@ -510,14 +628,9 @@ def run_extras(device, steps=20):
                                    backend="cute")
         return torch.autograd.grad((q_, k_, p[:, :, 2].transpose(1, 2)), (xg, wg, wr, sr), ups)
 
-    step = {"fused_ms": round(_event_ms(step_fused, steps), 4),
-            "cublas_linear_and_prologue_ms": round(_event_ms(step_composed, steps), 4)}
-    step["speedup"] = round(step["cublas_linear_and_prologue_ms"] / step["fused_ms"], 3)
-    step["flop"] = 3 * flop
-    step["note"] = ("forward + backward to x, W, rmsnorm_weight, scales; 3 GEMMs of 2*M*N*K each; "
-                    "composed = F.linear (cuBLAS) + qknorm_rope_scale(cute) + autograd")
-    out["c5_training_step"] = step
-    del gq5, gk5, gv5, dp, xg, wg
+    out["c5_step"] = {"fused_ms": r4(_event_ms(step_fused, steps)),
+                      "composed_ms": r4(_event_ms(step_composed, steps))}
+    del gq5, gk5, gv5, xg, wg
     return out
 
 
@@ -528,7 +641,7 @@ def _measured(key, fallback):
         return fallback
 
 
-def run_e2e(args, T, device, w, s, world):
+def run_e2e(args, T, device, w, s, world, local):
     """Same metric with pinned host buffers: H2D inputs + D2H outputs inside the timing.
 
     Every step copies its inputs host->device, runs the public API forward +
@@ -590,10 +703,46 @@ def run_e2e(args, T, device, w, s, world):
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(end), world) / steps
     gbs = world * tok * (FWD_BYTES_PER_TOKEN + BWD_BYTES_PER_TOKEN) / (ms * 1e-3) / 1e9
+    # What bounds it: this rank's pinned-host copy bandwidth in each direction
+    # alone (the step's own upload / download bytes, one direction at a time),
+    # min over ranks, and where the GPU sits (its NUMA node).
+    up = _copy_gbs(dev_in[0], host_in, steps=3)
+    down = _copy_gbs(host_out[0], [t for t in dev_in[0][:4]] + [w.detach().reshape(-1), s.detach().reshape(-1)],
+                     steps=3, to_host=True)
     return {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3), "tokens_per_step": tok,
-            "path": "qknorm_rope_scale(backend='cute') -> torch.library op -> C ABI; steps pipelined "
-                    "over two buffer sets (H2D, compute, D2H on separate streams)"}
+            "h2d_gbs_min": round(min_over_ranks(up, world), 1),
+            "d2h_gbs_min": round(min_over_ranks(down, world), 1),
+            "numa_node": _numa_node(local),
+            "path": "public API, pinned host buffers, 2 buffer sets, H2D/compute/D2H on 3 streams"}
+
+
+def _copy_gbs(dsts, srcs, steps=3, to_host=False):
+    """GB/s of copying srcs into dsts (one direction), CUDA events on the current stream."""
+    nbytes = sum(t.numel() * t.element_size() for t in (srcs if not to_host else dsts))
+    pairs = list(zip(dsts, srcs))
+
+    def run():
+        for d, h in pairs:
+            if d.numel() == h.numel():
+                d.view(-1).copy_(h.reshape(-1), non_blocking=True)
+
+    ms = _event_ms(run, steps, warmup=1)
+    return nbytes / (ms * 1e-3) / 1e9
+
+
+def _numa_node(local):
+    """NUMA node of the GPU's PCI device (sysfs), or None."""
+    try:
+        out = subprocess.run(["nvidia-smi", f"--id={local}", "--query-gpu=pci.bus_id",
+                              "--format=csv,noheader"], capture_output=True, text=True, timeout=10)
+        bus = out.stdout.strip()
+        bus = bus.lower()
+        if bus.count(":") == 2 and len(bus.split(":")[0]) == 8:
+            bus = bus[4:]  # 00000000:18:00.0 -> 0000:18:00.0
+        return int(Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text().strip())
+    except Exception:
+        return None
 
 
 def run_c5_profile_case(T):
@@ -642,7 +791,8 @@ def main():
     ap.add_argument("--cpu-reps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip the C1/C3/C4/C5 timings reported beside the headline")
+                    help="skip the C1/inverse/QKV-step/C5 timings reported beside the headline")
+    ap.add_argument("--detail", default="", help="also write the JSON line, indented, to this file")
     ap.add_argument("--c5-profile-tokens", type=int, default=0,
                     help="only run the fused QKV GEMM + prologue (C5 shapes, this many tokens) three "
                          "times and exit: the small case an ncu capture of that kernel uses")
