@@ -53,6 +53,27 @@ __global__ void __launch_bounds__(256) copy_rows_kernel(const CopyArgs a) {
   }
 }
 
+// [first, last] bytes a view touches: base plus each outer dimension's extent
+// times the magnitude of its stride (negative strides reach below the base).
+void byte_span(const void* base, const int64_t strides[3], const int64_t dims[3], int64_t row_bytes,
+               uintptr_t* lo, uintptr_t* hi) {
+  int64_t below = 0, above = row_bytes - 1;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t reach = (dims[i] - 1) * strides[i];
+    if (reach < 0) below += reach; else above += reach;
+  }
+  *lo = reinterpret_cast<uintptr_t>(base) + below;
+  *hi = reinterpret_cast<uintptr_t>(base) + above;
+}
+
+bool byte_span_overlap(const void* src, const int64_t ss[3], const void* dst, const int64_t ds[3],
+                       const int64_t dims[3], int64_t row_bytes) {
+  uintptr_t slo, shi, dlo, dhi;
+  byte_span(src, ss, dims, row_bytes, &slo, &shi);
+  byte_span(dst, ds, dims, row_bytes, &dlo, &dhi);
+  return slo <= dhi && dlo <= shi;
+}
+
 }  // namespace
 }  // namespace flash_prologue
 
@@ -76,6 +97,10 @@ FLASH_PROLOGUE_API int flash_prologue_copy_rows(const void* src, const int64_t s
   for (int i = 0; i < 3; ++i)
     if ((dims[i] > 1 && ((src_strides[i] | dst_strides[i]) & 15) != 0))
       return FLASH_PROLOGUE_ERR_ALIGNMENT;
+  // src is read through the read-only (non-coherent) path while dst is written,
+  // so the two must not overlap: byte ranges that do are rejected.
+  if (byte_span_overlap(src, src_strides, dst, dst_strides, dims, row_bytes))
+    return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   CopyArgs a{};
   a.src = static_cast<const char*>(src);
   a.dst = static_cast<char*>(dst);

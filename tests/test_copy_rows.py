@@ -21,6 +21,17 @@ def test_c_abi_argument_checks():
     assert lib.flash_prologue_copy_rows(p, s3, p, s3, dims, 24, None) == _lib.ERR_ALIGNMENT
     assert lib.flash_prologue_copy_rows(p, s3, p, s3, None, 128, None) == _lib.ERR_INVALID_ARGUMENT
     assert lib.flash_prologue_copy_rows(p, s3, p, s3, (ctypes.c_int64 * 3)(1, 0, 4), 128, None) == _lib.OK
+    # overlapping source and destination byte ranges are rejected before any launch:
+    # 4 rows of 128 B at stride 128 from 4096 (bytes 4096..4607) against the same
+    # layout from 4352 or from 3712
+    base, s_row = ctypes.c_void_p(4096), (ctypes.c_int64 * 3)(0, 0, 128)
+    for dst in (4096 + 256, 4096 - 384):
+        assert lib.flash_prologue_copy_rows(base, s_row, ctypes.c_void_p(dst), s_row, dims, 128,
+                                            None) == _lib.ERR_INVALID_ARGUMENT
+    # a reversed stride reaches below the base: rows at 5120, 4992, 4864, 4736 (bytes 4736..5247)
+    neg = (ctypes.c_int64 * 3)(0, 0, -128)
+    assert lib.flash_prologue_copy_rows(ctypes.c_void_p(5120), neg, ctypes.c_void_p(4096 + 512), s_row, dims,
+                                        128, None) == _lib.ERR_INVALID_ARGUMENT
     with pytest.raises(ValueError, match="CUDA"):
         _lib.copy_rows(torch.empty(4, 8), torch.empty(4, 8))
 
