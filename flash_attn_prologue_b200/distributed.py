@@ -43,9 +43,9 @@ def reduce_param_grads(dw: torch.Tensor, ds: torch.Tensor, group: Optional[dist.
     if world == 1:
         return unpack_param_grads(flat, dw, ds)
     if deterministic:
-        gathered = torch.empty((world, flat.numel()), dtype=flat.dtype, device=flat.device)
+        gathered = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
         dist.all_gather_into_tensor(gathered, flat, group=group)
-        total = gathered.sum(0)
+        total = gathered.view(world, flat.numel()).sum(0)
     else:
         total = flat
         dist.all_reduce(total, op=dist.ReduceOp.SUM, group=group)
@@ -76,9 +76,12 @@ class ParamGradReducer:
         self.stream.wait_stream(main)
         with torch.cuda.stream(self.stream):
             out = reduce_param_grads(dw, ds, self.group, self.deterministic)
-        # The partials were allocated on the main stream and are read here.
+        # The partials were allocated on the main stream and are read here; the
+        # results, allocated here, are read on the main stream after wait().
         dw.record_stream(self.stream)
         ds.record_stream(self.stream)
+        for t in out:
+            t.record_stream(main)
         return out
 
     def wait(self):

@@ -2,7 +2,7 @@
 
 Covers the only collective of the path: the sum over ranks of d rmsnorm_weight
 and d scales (flash_attn_prologue_b200/distributed.py), in its deterministic
-(all_gather + rank-order sum) and all_reduce forms, the token sharding helper,
+(all_gather + one column sum, identical bits on every rank) and all_reduce forms, the token sharding helper,
 the sharded-equals-unsharded property of the whole forward/backward, and a
 failure made on the host: a rank that leaves before the collective must make
 its peer fail with an error instead of hanging.
@@ -78,6 +78,41 @@ def test_param_grad_reduction_two_ranks():
         torch.testing.assert_close(dw_ar, exp_dw, rtol=1e-6, atol=1e-6)
         torch.testing.assert_close(ds_ar, exp_ds, rtol=1e-6, atol=1e-6)
     assert torch.equal(results[0][1], results[1][1]) and torch.equal(results[0][2], results[1][2])
+
+
+def _worker_three(rank, world, port, out):
+    """Three ranks: the deterministic reduction gives the same bits on every rank, and
+    ParamGradReducer (synchronous on CPU tensors) returns what reduce_param_grads does."""
+    try:
+        _init(rank, world, port)
+        from flash_attn_prologue_b200.distributed import ParamGradReducer
+        g = torch.Generator().manual_seed(200 + rank)
+        dw = torch.randn(2, 1, 32, generator=g)
+        ds = torch.randn(8, 1, 1, generator=g)
+        a = reduce_param_grads(dw, ds)
+        reducer = ParamGradReducer()
+        b = reducer.reduce(dw, ds)
+        reducer.wait()
+        out.put((rank, a[0], a[1], b[0], b[1], None))
+        dist.destroy_process_group()
+    except Exception:
+        out.put((rank, None, None, None, None, traceback.format_exc()))
+
+
+def test_three_ranks_identical_bits_and_side_stream_reducer():
+    results = _run(_worker_three, 3)
+    for r in results:
+        assert r[-1] is None, r[-1]
+    exp_dw, exp_ds = 0, 0
+    for r in range(3):
+        g = torch.Generator().manual_seed(200 + r)
+        exp_dw = exp_dw + torch.randn(2, 1, 32, generator=g)
+        exp_ds = exp_ds + torch.randn(8, 1, 1, generator=g)
+    for rank, dw, ds, rdw, rds, _ in results:
+        assert torch.equal(dw, results[0][1]) and torch.equal(ds, results[0][2])
+        assert torch.equal(rdw, dw) and torch.equal(rds, ds)
+        torch.testing.assert_close(dw, exp_dw, rtol=1e-6, atol=1e-6)
+        torch.testing.assert_close(ds, exp_ds, rtol=1e-6, atol=1e-6)
 
 
 def _worker_sharded(rank, world, port, out):
