@@ -102,12 +102,17 @@ constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + kEpiWarps *
 
 // Output tile, reduction range and chunk of a work unit (chunk-major, then
 // tiles with the hidden tile fastest, so clusters working at the same time
-// share their A rows and reduction range through L2).
+// share their A rows and reduction range through L2). Units of odd rounds
+// (u / n_pairs odd: the cluster's every second unit) walk the reduction
+// backwards, so a round starts on the operand blocks the previous round
+// read last, which are still in L2. The direction is fixed by u and the
+// grid, so results do not change run to run.
 struct Unit {
   int64_t tm, tn, kb_lo, kb_hi;
   int chunk;
+  bool reverse;  // walk the reduction from kb_hi - 1 down to kb_lo
 };
-__device__ __forceinline__ Unit unit_of(const BwdGemmArgs& a, int64_t u) {
+__device__ __forceinline__ Unit unit_of(const BwdGemmArgs& a, int64_t u, int64_t n_pairs) {
   Unit r;
   r.chunk = (int)(u / a.tiles);
   const int64_t tile = u % a.tiles;
@@ -115,6 +120,7 @@ __device__ __forceinline__ Unit unit_of(const BwdGemmArgs& a, int64_t u) {
   r.tn = tile % a.tiles_n;
   r.kb_lo = a.n_kb * r.chunk / a.split;
   r.kb_hi = a.n_kb * (r.chunk + 1) / a.split;
+  r.reverse = ((u / n_pairs) & 1) != 0;
   return r;
 }
 
@@ -175,10 +181,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int i = 0; i < 3; ++i) prefetch_tmap(&maps.grad[i]);
       prefetch_tmap(&maps.bop);
       const uint32_t full0 = mapa_shared(smem_u32(sm.full), 0);
+      // dX: every cluster reads all of W (25 MB at C5) again for each of its
+      // tiles; kept in L2 ahead of the streamed gradients.
+      const uint64_t pol_w = policy_evict_last();
       bool failed = false;
       uint32_t it = 0;
       for (int64_t u = pair; u < a.units && !failed; u += n_pairs) {
-        const Unit un = unit_of(a, u);
+        const Unit un = unit_of(a, u, n_pairs);
         const int32_t col0 = (int32_t)(un.tn * kBN + rank * 128);  // hidden column of B
         // dX: this CTA's 128 tokens; dW: this CTA's 128 rows of 3HD (two boxes).
         int32_t b_x = 0, n0 = 0;
@@ -192,7 +201,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // multiple of 256), one D = 128 head or two D = 64 heads.
           split_row(a, un.tm * kBN + rank * 128, s0, h0, d0);
         }
-        for (int64_t kb = un.kb_lo; kb < un.kb_hi; ++kb, ++it) {
+        for (int64_t j = 0; j < un.kb_hi - un.kb_lo; ++j, ++it) {
+          const int64_t kb = un.reverse ? un.kb_hi - 1 - j : un.kb_lo + j;
           const int s = it % kStages;
           if (!mbar_wait(&sm.empty[s], ((it / kStages) & 1) ^ 1)) { failed = true; break; }
           unsigned char* st = sm.ring + s * kStageBytes;
@@ -204,7 +214,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int32_t h, d;
             split_row(a, kb * kBK, slot, h, d);
             tma_load_5d_pair(st, &maps.grad[slot], 0, n0, d / 64, h, b_x, bar);
-            tma_load_3d_pair(st + kStageA, &maps.bop, 0, (int32_t)(kb * kBK), col0 / 64, bar);
+            tma_load_3d_pair_hint(st + kStageA, &maps.bop, 0, (int32_t)(kb * kBK), col0 / 64, bar, pol_w);
           } else {
             const int32_t bb = (int32_t)(kb / a.kb_per_batch);
             const int32_t t0 = (int32_t)((kb % a.kb_per_batch) * kBK);
@@ -231,12 +241,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool failed = false;
       uint32_t it = 0, tcount = 0;
       for (int64_t u = pair; u < a.units && !failed; u += n_pairs, ++tcount) {
-        const Unit un = unit_of(a, u);
+        const Unit un = unit_of(a, u, n_pairs);
         const uint32_t abuf = tcount & 1;
         if (!mbar_wait_cluster(&sm.acc_empty[abuf], ((tcount >> 1) & 1) ^ 1)) { failed = true; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + abuf * kAccCols;
-        for (int64_t kb = un.kb_lo; kb < un.kb_hi; ++kb, ++it) {
+        for (int64_t j = 0; j < un.kb_hi - un.kb_lo; ++j, ++it) {
           const int s = it % kStages;
           if (!mbar_wait(&sm.full[s], (it / kStages) & 1)) { failed = true; break; }
           tc_fence_after();
@@ -250,7 +260,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                        ? smem_desc_k_sw128(sa + (kk >> 2) * kBlock) + 2 * (kk & 3)
                                        : smem_desc_mn_sw128(sa + kk * 2048, kBlock);
             const uint64_t bdesc = smem_desc_mn_sw128(sb + kk * 2048, kBlock);
-            umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb != un.kb_lo || kk != 0) ? 1u : 0u);
+            umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (j != 0 || kk != 0) ? 1u : 0u);
           }
           umma_commit_pair(empty_own + s * kBar);
           umma_commit_pair(empty_peer + s * kBar);
@@ -290,7 +300,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     };
     uint32_t tcount = 0;
     for (int64_t u = pair; u < a.units; u += n_pairs, ++tcount) {
-      const Unit un = unit_of(a, u);
+      const Unit un = unit_of(a, u, n_pairs);
       const uint32_t abuf = tcount & 1;
       if (!mbar_wait(&sm.acc_full[abuf], (tcount >> 1) & 1)) break;
       tc_fence_after();

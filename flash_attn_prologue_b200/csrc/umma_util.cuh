@@ -297,6 +297,17 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m
         "r"(bar)
       : "memory");
 }
+// tma_load_3d_pair with an L2 eviction policy (createpolicy) for the loaded lines.
+__device__ __forceinline__ void tma_load_3d_pair_hint(void* dst, const CUtensorMap* map, int32_t c0,
+                                                      int32_t c1, int32_t c2, uint32_t bar,
+                                                      uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+        "r"(bar), "l"(policy)
+      : "memory");
+}
 __device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, int32_t c0,
                                                  int32_t c1, int32_t c2, int32_t c3, uint32_t bar) {
   asm volatile(
