@@ -11,11 +11,9 @@
 //                    product equals the one dx needs anyway)
 //   d w[t][j]     += dn_j * n_j
 //   dx_j = r * (dn_j w_j - n_j * sum_i(dn_i w_i n_i) / D)
-// evaluated with e folded into r: with d0 = R^T g, u = d0 w and re = r e,
-// dn = e d0, d w += (d0 x) re, the row sum is re sum_i u_i x_i, and
-// dx = re u - x r^2 (sum / D). The sum of squares and sum_i u_i x_i need no r,
-// so bwd_lane_pre forms both (and u, d0 x) before either row reduction, the
-// two reduce in one interleaved butterfly, and bwd_lane_finish applies r.
+// evaluated with e folded into r (bwd_lane_reduce / lane_dx): with
+// d0 = R^T g, re = r e and n' = x re, dn = e d0, d w += d0 n', the row sum is
+// sum_i d0_i w_i n'_i, and dx = re (d0 w) - n' (r sum / D) / e.
 // The reference accumulates the two parameter gradients with float atomics
 // (fused_epilogue.py:1129-1207), whose order changes run to run. Here every
 // CTA owns fixed rows (persistent, round-robin items); its threads keep
@@ -120,7 +118,7 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
       }
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
       float2 dnw1[kPairs], dnw2[kPairs];  // u = d0 w (INV: t = d0 w)
-      float2 n1[kPairs], n2[kPairs];      // t = d0 x; INV: n' = e n rebuilt from the outputs
+      float2 n1[kPairs], n2[kPairs];      // n' = e n: x re, or rebuilt from the outputs (INV)
       float r, re, dsum;
       if constexpr (INV) {
         r = ok ? __ldg(rms + (b * a.H + h) * a.N + n) : 0.f;
@@ -132,11 +130,10 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
         }
         dsum = row_sum<L>(part);
       } else {
-        const float2 sums = row_sum2<L>(bwd_lane_pre(x1, x2, g1, g2, w + j0, w + HALF + j0, sn, cs, dnw1,
-                                                     dnw2, n1, n2));
-        r = inv_rms_bwd<D>(sums.x, a.eps);
+        r = inv_rms_bwd<D>(row_sum<L>(lane_sumsq2(x1, x2)), a.eps);
         re = __fmul_rn(r, e);
-        dsum = __fmul_rn(re, sums.y);
+        dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, re, w + j0, w + HALF + j0, sn, cs, acc1p,
+                                          acc2p, dnw1, dnw2, n1, n2));
       }
       if (t == 0) {
         // d scales: the row's sum(dn w n), reduced over the warp's position slots.
@@ -152,8 +149,8 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
                        __fmul_rn(__fmul_rn(r, dsum * (1.0f / (float)D)), t == 0 ? ie_s[h] : 1.f),
                        out1, out2);
       else
-        bwd_lane_finish<T>(x1, x2, dnw1, dnw2, n1, n2, re, __fmul_rn(r, __fmul_rn(r, dsum * (1.0f / (float)D))),
-                           acc1p, acc2p, out1, out2);
+        lane_dx<T>(n1, n2, dnw1, dnw2, re, __fdividef(__fmul_rn(r, dsum * (1.0f / (float)D)), e), out1,
+                   out2);
       T* dp = db + b * sd.b + (int64_t)h * sd.h + n * sd.n + j0;
       store_stream<T, VEC>(dp, out1);
       store_stream<T, VEC>(dp + HALF, out2);

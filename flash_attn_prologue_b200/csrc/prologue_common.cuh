@@ -298,6 +298,21 @@ __device__ __forceinline__ float lane_sumsq(const Chunk<T>& x1, const Chunk<T>& 
   return __fadd_rn(acc.x, acc.y);
 }
 
+// lane_sumsq with the two halves summed in independent chains (backward only:
+// its r carries no bit-parity requirement, and the shorter chain hides latency).
+template <typename T>
+__device__ __forceinline__ float lane_sumsq2(const Chunk<T>& x1, const Chunk<T>& x2) {
+  float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int p = 0; p < kPairs; ++p) {
+    const float2 u = chunk_get2(x1, p), v = chunk_get2(x2, p);
+    a = (sizeof(T) == 2) ? __ffma2_rn(u, u, a) : __fadd2_rn(a, __fmul2_rn(u, u));
+    b = (sizeof(T) == 2) ? __ffma2_rn(v, v, b) : __fadd2_rn(b, __fmul2_rn(v, v));
+  }
+  const float2 s = __fadd2_rn(a, b);
+  return __fadd_rn(s.x, s.y);
+}
+
 // Forward outputs of one lane: normed = (x * r) * w, rotated, times e for Q.
 // Every product and sum rounds separately, as in the eager formulation
 // (a - b is computed as a + (-b), which rounds identically).
@@ -325,79 +340,47 @@ __device__ __forceinline__ void fwd_lane(const Chunk<T>& x1, const Chunk<T>& x2,
   chunk_set2(out2, o2);
 }
 
-// Backward of one lane, the part that does not need the row statistic r.
-// With d0 = R^T g (the inverse rotation of the upstream gradient, without the
-// Q scale e) and u = d0 w, the lane keeps u and t = d0 x and returns its
-// partials of the two row sums
-//   .x = sum_j x_j^2        (r = 1 / sqrt(mean + eps))
-//   .y = sum_j u_j x_j      (times r e: <dn, n>, the row's d scale term)
-// Both sums then reduce across the row's lanes together (row_sum2), and
-// bwd_lane_finish applies r. Nothing here waits on a reduction, so the row's
-// arithmetic runs ahead of its butterflies. Independent partial sums for the
-// two halves shorten the dependency chains.
+// Backward, reduction part of one lane. With d0 = R^T g (the inverse rotation
+// of the upstream gradient, without the Q scale e) and re = r * e (r for K):
+// dy = e d0 is the gradient of the normed row n w and dn = dy w = e u with
+// u = d0 w, so
+//   d w partial:  acc += d0 * (x re)                        (= dy n)
+//   returned:     lane partial of sum_j u_j (x_j re)        (= <dn, n>)
+// and u is kept for the dx part. The returned sum is also the row's
+// contribution to d scale: <dn, n> = <R^T g', n w> = <g', R(n w)> =
+// sum_j dq_out_j q_out_j. The lane keeps n' = x re for the dx part (lane_dx),
+// so x is not unpacked again. Two independent partial sums (first / second
+// half) shorten the dependency chain.
 template <typename T>
-__device__ __forceinline__ float2 bwd_lane_pre(const Chunk<T>& x1, const Chunk<T>& x2,
-                                               const Chunk<T>& g1, const Chunk<T>& g2,
-                                               const float* wa, const float* wb,
-                                               const float (&sn)[kChunk], const float (&cs)[kChunk],
-                                               float2 (&u1)[kPairs], float2 (&u2)[kPairs],
-                                               float2 (&t1)[kPairs], float2 (&t2)[kPairs]) {
-  float2 ss1 = make_float2(0.f, 0.f), ss2 = make_float2(0.f, 0.f);
-  float2 ux1 = make_float2(0.f, 0.f), ux2 = make_float2(0.f, 0.f);
+__device__ __forceinline__ float bwd_lane_reduce(const Chunk<T>& x1, const Chunk<T>& x2,
+                                                 const Chunk<T>& g1, const Chunk<T>& g2, float re,
+                                                 const float* wa, const float* wb,
+                                                 const float (&sn)[kChunk], const float (&cs)[kChunk],
+                                                 float2 (&acc1)[kPairs], float2 (&acc2)[kPairs],
+                                                 float2 (&u1)[kPairs], float2 (&u2)[kPairs],
+                                                 float2 (&nx1)[kPairs], float2 (&nx2)[kPairs]) {
+  const float2 re2 = splat2(re);
+  float2 ds1 = make_float2(0.f, 0.f), ds2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int p = 0; p < kPairs; ++p) {
     const float2 c2 = make_float2(cs[2 * p], cs[2 * p + 1]);
     const float2 s2 = make_float2(sn[2 * p], sn[2 * p + 1]);
-    const float2 xa = chunk_get2(x1, p), xb = chunk_get2(x2, p);
     const float2 ga = chunk_get2(g1, p), gb = chunk_get2(g2, p);
-    ss1 = (sizeof(T) == 2) ? __ffma2_rn(xa, xa, ss1) : __fadd2_rn(ss1, __fmul2_rn(xa, xa));
-    ss2 = (sizeof(T) == 2) ? __ffma2_rn(xb, xb, ss2) : __fadd2_rn(ss2, __fmul2_rn(xb, xb));
     const float2 d1 = __ffma2_rn(ga, c2, __fmul2_rn(gb, s2));
     const float2 d2 = __ffma2_rn(gb, c2, neg2(__fmul2_rn(ga, s2)));
+    const float2 n1 = __fmul2_rn(chunk_get2(x1, p), re2);
+    const float2 n2 = __fmul2_rn(chunk_get2(x2, p), re2);
+    nx1[p] = n1;
+    nx2[p] = n2;
+    acc1[p] = __ffma2_rn(d1, n1, acc1[p]);
+    acc2[p] = __ffma2_rn(d2, n2, acc2[p]);
     u1[p] = __fmul2_rn(d1, ld_pair(wa, p));
     u2[p] = __fmul2_rn(d2, ld_pair(wb, p));
-    t1[p] = __fmul2_rn(d1, xa);
-    t2[p] = __fmul2_rn(d2, xb);
-    ux1 = __ffma2_rn(u1[p], xa, ux1);
-    ux2 = __ffma2_rn(u2[p], xb, ux2);
+    ds1 = __ffma2_rn(u1[p], n1, ds1);
+    ds2 = __ffma2_rn(u2[p], n2, ds2);
   }
-  const float2 ss = __fadd2_rn(ss1, ss2), ux = __fadd2_rn(ux1, ux2);
-  return make_float2(__fadd_rn(ss.x, ss.y), __fadd_rn(ux.x, ux.y));
-}
-
-// Sums of two values over the L lanes of a row (interleaved xor butterflies).
-template <int L>
-__device__ __forceinline__ float2 row_sum2(float2 v) {
-#pragma unroll
-  for (int o = 1; o < L; o <<= 1) {
-    const float a = __shfl_xor_sync(0xffffffffu, v.x, o);
-    const float b = __shfl_xor_sync(0xffffffffu, v.y, o);
-    v.x = __fadd_rn(v.x, a);
-    v.y = __fadd_rn(v.y, b);
-  }
-  return v;
-}
-
-// Backward of one lane once the row's r is known (re = r e, r for K):
-//   d w partial:  acc += t re                 (= d0 (x r e) = dy n)
-//   dx = re u - x k2,  k2 = r^2 <u, x> re / D   (= r (dn - n m), m = <dn, n> / D)
-template <typename T>
-__device__ __forceinline__ void bwd_lane_finish(const Chunk<T>& x1, const Chunk<T>& x2,
-                                                const float2 (&u1)[kPairs], const float2 (&u2)[kPairs],
-                                                const float2 (&t1)[kPairs], const float2 (&t2)[kPairs],
-                                                float re, float k2, float2 (&acc1)[kPairs],
-                                                float2 (&acc2)[kPairs], Chunk<T>& out1, Chunk<T>& out2) {
-  const float2 re2 = splat2(re), nk2 = splat2(-k2);
-  float2 o1[kPairs], o2[kPairs];
-#pragma unroll
-  for (int p = 0; p < kPairs; ++p) {
-    acc1[p] = __ffma2_rn(t1[p], re2, acc1[p]);
-    acc2[p] = __ffma2_rn(t2[p], re2, acc2[p]);
-    o1[p] = __ffma2_rn(chunk_get2(x1, p), nk2, __fmul2_rn(re2, u1[p]));
-    o2[p] = __ffma2_rn(chunk_get2(x2, p), nk2, __fmul2_rn(re2, u2[p]));
-  }
-  chunk_set2(out1, o1);
-  chunk_set2(out2, o2);
+  const float2 ds = __fadd2_rn(ds1, ds2);
+  return __fadd_rn(ds.x, ds.y);
 }
 
 // ---------------------------------------------------------------------------

@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       const int h = a.p.heads_inner ? tc.i0 + i_l : tc.o0 + o_l;
       const float e = (t == 0 && h < a.H) ? e_s[h] : 1.f;
       float2 dnw1[kPairs], dnw2[kPairs];  // u = d0 w (INV: t = d0 w)
-      float2 n1[kPairs], n2[kPairs];      // t = d0 x; INV: n' = e n rebuilt from the outputs
+      float2 n1[kPairs], n2[kPairs];      // n' = e n: x re, or rebuilt from the outputs (INV)
       float rr, re, dsum;
       if constexpr (INV) {
         rr = pass == 0 ? rv0 : rv1;
@@ -416,10 +416,10 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
         }
         dsum = row_sum<L>(part);
       } else {
-        const float2 sums = row_sum2<L>(bwd_lane_pre(x1, x2, g1, g2, wa, wb, sn, cs, dnw1, dnw2, n1, n2));
-        rr = inv_rms_bwd<D>(sums.x, a.eps);
+        rr = inv_rms_bwd<D>(row_sum<L>(lane_sumsq2(x1, x2)), a.eps);
         re = __fmul_rn(rr, e);
-        dsum = __fmul_rn(re, sums.y);
+        dsum = row_sum<L>(bwd_lane_reduce(x1, x2, g1, g2, re, wa, wb, sn, cs, acc1p, acc2p, dnw1,
+                                          dnw2, n1, n2));
       }
       if (t == 0) {
         float v = dsum;
@@ -434,8 +434,8 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
                        __fmul_rn(__fmul_rn(rr, dsum * (1.0f / (float)D)), t == 0 ? ie_s[h] : 1.f),
                        out1, out2);
       else
-        bwd_lane_finish<T>(x1, x2, dnw1, dnw2, n1, n2, re, __fmul_rn(rr, __fmul_rn(rr, dsum * (1.0f / (float)D))),
-                           acc1p, acc2p, out1, out2);
+        lane_dx<T>(n1, n2, dnw1, dnw2, re, __fdividef(__fmul_rn(rr, dsum * (1.0f / (float)D)), e), out1,
+                   out2);
       T* dp = dtile + (int64_t)i_l * sd_inner + (int64_t)o_l * sd_outer;
       store_stream<T, true>(dp, out1);
       store_stream<T, true>(dp + HALF, out2);
