@@ -51,8 +51,9 @@ BWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 6 + HEAD_DIM * 4
 # the algorithmic bytes.
 NCU_TRAFFIC_BYTES_PER_TOKEN = {"fwd": 8018, "bwd": 12131}
 # sm__pipe_tensor_cycles_active (% of active cycles) of the fused QKV GEMM +
-# prologue kernel in one ncu capture at C5 size (summary kept under profiles/).
-NCU_C5_TENSOR_ACTIVE_PCT = 77.1
+# prologue kernel in one ncu capture at C5's full size (summary kept under
+# profiles/qkv_gemm_pair_c5_t65536.md).
+NCU_C5_TENSOR_ACTIVE_PCT = 80.9
 
 
 def measured_peak():
