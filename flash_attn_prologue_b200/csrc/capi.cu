@@ -197,8 +197,8 @@ int common_checks(const void* q, const int64_t* qs, const void* k, const int64_t
 // 0: automatic (TMA pipeline when the layout allows it), 1: register path only.
 int g_path_mode = 0;
 
-constexpr int kFwdStages = 3;
-constexpr int kBwdStages = 3;
+constexpr int kFwdStages = kTmaFwdStages;
+constexpr int kBwdStages = kTmaBwdStages;
 
 // A streamed input the TMA path can read: 16-byte aligned, rows along the
 // inner dim contiguous (stride D), positive b and outer strides that are

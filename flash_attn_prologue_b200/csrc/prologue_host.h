@@ -73,6 +73,11 @@ struct BwdArgs {
 constexpr int kTmaConsumerWarps = 8;                       // 0-3: Q rows, 4-7: K rows
 constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kTmaTileBytes = 8192;                        // per streamed tensor per stage
+// Pipeline stages of the forward / backward kernels. Compile-time, so the
+// kernels' stage index and barrier phase (k % S, k / S) cost a multiply and a
+// shift instead of an integer division per tile.
+constexpr int kTmaFwdStages = 3;
+constexpr int kTmaBwdStages = 3;
 
 // Bytes of one pipeline stage: `nt` streamed tiles, then the sin and cos rows,
 // rounded up so that every stage (each TMA destination) stays 128-byte aligned.

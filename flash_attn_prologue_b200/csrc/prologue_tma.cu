@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   constexpr int HALF = S_::HALF;
   constexpr int L = S_::L;
   extern __shared__ __align__(128) unsigned char smem[];
-  const int S = a.p.stages;
+  constexpr int S = kTmaFwdStages;  // == a.p.stages (the host plans with the same constant)
   const int table_bytes = a.p.P * HALF * 4;
   const int r_off = tma_stage_bytes(2, table_bytes);  // RMS: the tile's r values
   const int stage_bytes = r_off + (RMS ? tma_r_area_bytes(S_::ROWS) : 0);
@@ -270,7 +270,10 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
   constexpr int L = S_::L;
   constexpr int LOG2_L = S_::LOG2_L;
   extern __shared__ __align__(128) unsigned char smem[];
-  const int S = a.p.stages;
+  // Compile-time for the regular backward (2.4% faster at C2); the inverse
+  // backward keeps the runtime value, whose division costs less there than
+  // the register spill the constant caused (15% slower when measured).
+  const int S = INV ? a.p.stages : kTmaBwdStages;  // == a.p.stages
   const int table_bytes = a.p.P * HALF * 4;
   const int stage_bytes = tma_stage_bytes(4, table_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
