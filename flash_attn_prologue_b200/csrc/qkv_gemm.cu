@@ -235,19 +235,28 @@ __device__ __forceinline__ void run_epilogue(const OutMaps& om, const GemmArgs& 
       for (int j = 0; j < 16; ++j) { sn[slot][j] = 0.f; cs[slot][j] = 0.f; }
     }
   };
+  // Tile and token indices in 32-bit arithmetic (the host checks that tiles,
+  // tokens and M * H stay below 2^31): a 64-bit division is a long software
+  // sequence, and this runs once per tile in every epilogue thread.
+  const uint32_t n_tn = (uint32_t)a.n_tiles_n;
+  const uint32_t s32 = (uint32_t)a.S;
+  const uint32_t tiles_per_seg = (uint32_t)(a.H * D / BN);  // H * D is a multiple of BN
   uint32_t tcount = 0;
   for (int64_t tile = tile0; tile < a.n_tiles; tile += step, ++tcount) {
     const uint32_t abuf = tcount & 1;
-    const int64_t mrow0 = (tile / a.n_tiles_n) * ROWS + m_off;
-    const int64_t m = mrow0 + row;
-    valid = m < a.M;
-    const int64_t b = m / a.S, sp = m % a.S;
+    const uint32_t tm = (uint32_t)tile / n_tn, tn = (uint32_t)tile - tm * n_tn;
+    const uint32_t mrow0 = tm * ROWS + (uint32_t)m_off;
+    const uint32_t m = mrow0 + row;
+    valid = (int64_t)m < a.M;
+    const uint32_t b32 = m / s32;
+    const int64_t b = b32, sp = m - b32 * s32;
     // First token of this warp's 32 rows (S % 32 == 0 on the staged path,
     // so all 32 share its batch index).
-    const int64_t mw = mrow0 + quarter * 32;
-    const int64_t bw = mw / a.S, spw = mw % a.S;
-    const int64_t n0 = (tile % a.n_tiles_n) * BN;
-    const int seg = (int)(n0 / (a.H * D));  // the whole tile is Q (0), K (1) or V (2)
+    const uint32_t mw = mrow0 + quarter * 32;
+    const uint32_t bw32 = mw / s32;
+    const int64_t bw = bw32, spw = mw - bw32 * s32;
+    const int seg = (int)(tn / tiles_per_seg);  // the whole tile is Q (0), K (1) or V (2)
+    const int hbase = (int)(tn - (uint32_t)seg * tiles_per_seg) * HEADS_PER_TILE;  // its first head
     const bool prologue = a.apply_prologue && seg < 2;
     float e_first = 1.f;  // exp(scale) of this warp's first head of the tile (Q tiles)
     if (prologue) {
@@ -255,14 +264,14 @@ __device__ __forceinline__ void run_epilogue(const OutMaps& om, const GemmArgs& 
       crow = a.cos + b * a.cos_b + sp * a.cos_n;
 #pragma unroll
       for (int g = 0; g < SLOTS; ++g) load_group(g, g);
-      if (seg == 0) e_first = (float)exp((double)a.scales[((n0 + head0 * D) % (a.H * D)) / D]);
+      if (seg == 0) e_first = (float)exp((double)a.scales[hbase + head0]);
     }
     if (!mbar_wait(&sm.acc_full[abuf], (tcount >> 1) & 1)) break;
     tc_fence_after();
     const uint32_t tbase = tmem_base + abuf * kAccCols + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
     for (int hh = head0; hh < HEADS_PER_TILE; hh += HEAD_STEP) {
-      const int h = (int)(((n0 + hh * D) % (a.H * D)) / D);
+      const int h = hbase + hh;
       const uint32_t tcol = tbase + hh * D;
       const int64_t out_off = ((b * a.H + h) * a.S + sp) * D;
       const int64_t row0 = (bw * a.H + h) * a.S + spw;  // staged path: first output row

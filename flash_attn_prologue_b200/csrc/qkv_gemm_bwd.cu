@@ -112,15 +112,19 @@ struct Unit {
   int chunk;
   bool reverse;  // walk the reduction from kb_hi - 1 down to kb_lo
 };
+// Unit and row indices in 32-bit arithmetic: units, tiles, reduction blocks
+// and 3HD rows stay below 2^31 (checked on the host), and a 64-bit division is
+// a long software sequence.
 __device__ __forceinline__ Unit unit_of(const BwdGemmArgs& a, int64_t u, int64_t n_pairs) {
   Unit r;
-  r.chunk = (int)(u / a.tiles);
-  const int64_t tile = u % a.tiles;
-  r.tm = tile / a.tiles_n;
-  r.tn = tile % a.tiles_n;
+  const uint32_t u32 = (uint32_t)u, tiles = (uint32_t)a.tiles, tiles_n = (uint32_t)a.tiles_n;
+  const uint32_t chunk = u32 / tiles, tile = u32 - chunk * tiles;
+  r.chunk = (int)chunk;
+  r.tm = tile / tiles_n;
+  r.tn = tile - (uint32_t)r.tm * tiles_n;
   r.kb_lo = a.n_kb * r.chunk / a.split;
   r.kb_hi = a.n_kb * (r.chunk + 1) / a.split;
-  r.reverse = ((u / n_pairs) & 1) != 0;
+  r.reverse = ((u32 / (uint32_t)n_pairs) & 1) != 0;
   return r;
 }
 
@@ -131,11 +135,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 // (slot, head, first d) of row r of the [3HD] projection axis.
 __device__ __forceinline__ void split_row(const BwdGemmArgs& a, int64_t r, int& s, int32_t& h, int32_t& d) {
-  const int64_t hd = a.H * a.D;
-  s = (int)(r / hd);
-  const int64_t rem = r % hd;
-  h = (int32_t)(rem / a.D);
-  d = (int32_t)(rem % a.D);
+  const uint32_t hd = (uint32_t)(a.H * a.D), r32 = (uint32_t)r, dd = (uint32_t)a.D;
+  s = (int)(r32 / hd);
+  const uint32_t rem = r32 - (uint32_t)s * hd;
+  h = (int32_t)(rem / dd);
+  d = (int32_t)(rem - (uint32_t)h * dd);
 }
 
 }  // namespace
