@@ -276,7 +276,7 @@ def _timed_loop(fn, steps, warmup, world, finish=None):
 
 def run_ours(args, world, rank, local):
     from flash_attn_prologue_b200 import prepare_backend, qknorm_rope_scale
-    from flash_attn_prologue_b200.distributed import ParamGradReducer, reduce_param_grads
+    from flash_attn_prologue_b200.distributed import ParamGradReducer, PeerGroup
     prepare_backend("cute")
     device = torch.device("cuda", torch.cuda.current_device())
     T = args.tokens
@@ -286,7 +286,9 @@ def run_ours(args, world, rank, local):
     s.requires_grad_()
 
     stream = torch.cuda.current_stream()
-    reducer = ParamGradReducer(device=device) if world > 1 else None
+    peer = args.dp_reduce == "peer" and world > 1
+    reducer = ParamGradReducer(device=device) if world > 1 and not peer else None
+    peers = PeerGroup(device=device, max_cols=2 * HEAD_DIM + HEADS) if peer else None
     fwd_ev, bwd_ev, coll_ev = [], [], []
 
     def step(record=False):
@@ -297,7 +299,12 @@ def run_ours(args, world, rank, local):
         out = qknorm_rope_scale(qq, kk, w, s, sin, cos, backend="cute")
         if record:
             e1 = torch.cuda.Event(enable_timing=True); e1.record(stream)
-        dq, dk, dw, ds = torch.autograd.grad(out, (qq, kk, w, s), (gq, gk))
+        if peers is not None:
+            # d w / d s come out of the backward already summed over the ranks
+            with peers.reducing():
+                dq, dk, dw, ds = torch.autograd.grad(out, (qq, kk, w, s), (gq, gk))
+        else:
+            dq, dk, dw, ds = torch.autograd.grad(out, (qq, kk, w, s), (gq, gk))
         if record:
             e2 = torch.cuda.Event(enable_timing=True); e2.record(stream)
             fwd_ev.append((e0, e1))
@@ -348,7 +355,14 @@ def run_ours(args, world, rank, local):
     peak, peak_kind = measured_peak()
 
     coll = None
-    if world > 1:
+    if peers is not None:
+        from flash_attn_prologue_b200 import _lib
+        peer_error = int(max_over_ranks(float(_lib.device_error(reset=True)), world))
+        coll = {"how": "in the backward's finalize kernel: each rank's [2*D+H] sums written to every "
+                       "rank's exchange buffer over NVLink, flags, rank-order sum (bwd.ms includes it)",
+                "isolated_ms": round(isolated_peer_reduction_ms(device, world, peers), 4),
+                "floats": 2 * HEAD_DIM + HEADS, "device_error": peer_error}
+    elif world > 1:
         # The reduction alone: on its side stream inside the step (from the end of
         # the backward to the sum's completion, so it includes waiting for the
         # slowest rank), and isolated (back-to-back on the main stream).
@@ -360,6 +374,9 @@ def run_ours(args, world, rank, local):
                 "how": "pack + NCCL all_gather + column sum on a side stream; in_step spans the "
                        "end of the backward to the sum (it waits while the next forward holds the SMs)"}
     del buf, gq, gk
+    if peers is not None:
+        barrier(world)
+        peers.close()
 
     c4 = run_c4(args, device, world, rank, peak)
     c3 = run_c3(args, device, world, rank, peak)
@@ -405,6 +422,32 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line, separators=(",", ":")), flush=True)
     if args.detail and rank == 0:
         Path(args.detail).write_text(json.dumps(line, indent=1))
+
+
+def isolated_peer_reduction_ms(device, world, peers, reps=20):
+    """Device time of a 16-token backward inside peers.reducing() (its backward kernel
+    takes a few microseconds; the rest is the peer finalize), ranks aligned by a barrier
+    before each call."""
+    from flash_attn_prologue_b200 import qknorm_rope_scale
+    T = 16
+    buf, w, s, sin, cos, gq, gk = make_inputs(T, device, 7)
+    w.requires_grad_()
+    s.requires_grad_()
+    times = []
+    for i in range(reps + 3):
+        out = qknorm_rope_scale(buf[:, 0], buf[:, 1], w, s, sin, cos, backend="cute")
+        torch.cuda.synchronize()
+        barrier(world)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        with peers.reducing():
+            torch.autograd.grad(out, (w, s), (gq, gk))
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append(a.elapsed_time(b))
+    return max_over_ranks(statistics.median(times), world)
 
 
 def isolated_reduction_ms(device, world, reps=20):
@@ -814,6 +857,9 @@ def main():
     ap.add_argument("--e2e-tokens", type=int, default=T_TOKENS // 4)
     ap.add_argument("--cpu-tokens", type=int, default=32768)
     ap.add_argument("--cpu-reps", type=int, default=5)
+    ap.add_argument("--dp-reduce", choices=["nccl", "peer"], default="nccl",
+                    help="N > 1: sum d rmsnorm_weight / d scales with NCCL on a side stream, or "
+                         "inside the backward's finalize kernel over NVLink peer memory")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the C1/inverse/QKV-step/C5 timings reported beside the headline")

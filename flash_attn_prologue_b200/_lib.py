@@ -69,7 +69,28 @@ SIGNATURES = {
                             _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
                             _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64,
                             ctypes.c_float, ctypes.c_int, _vp], ctypes.c_int),
+    "flash_prologue_bwd_dp": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,
+                               _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
+                               _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64,
+                               ctypes.c_float, ctypes.c_int, _vp, ctypes.c_uint32, _vp], ctypes.c_int),
+    "flash_prologue_peer_buffer_bytes": ([ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t),
+                                          ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "flash_prologue_ipc_handle": ([_vp, _vp, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
+    "flash_prologue_ipc_open": ([_vp, _i64, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "flash_prologue_ipc_close": ([_vp, _i64], ctypes.c_int),
+    "flash_prologue_peer_reduce_emulated": ([_vp, _i64, ctypes.c_int32, ctypes.c_int32, _vp, _vp, _vp,
+                                             ctypes.c_uint32, _vp], ctypes.c_int),
 }
+
+MAX_PEERS = 8
+
+
+class PeersDesc(ctypes.Structure):
+    """flash_prologue_peers (include/flash_prologue.h): every rank's exchange
+    buffer and flag array as mapped in this process."""
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("max_cols", ctypes.c_int32),
+                ("wait_ms", ctypes.c_int32), ("data", ctypes.c_void_p * MAX_PEERS),
+                ("flags", ctypes.c_void_p * MAX_PEERS)]
 
 
 class PrologueError(RuntimeError):

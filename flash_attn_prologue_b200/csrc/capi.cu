@@ -240,12 +240,13 @@ extern "C" {
 
 FLASH_PROLOGUE_API int flash_prologue_device_error(int* value, int reset) {
   if (!value) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
-  int a = 0, b = 0, c = 0;
+  int a = 0, b = 0, c = 0, d = 0;
   if (read_device_error(&a, reset != 0) != cudaSuccess ||
       read_gemm_device_error(&b, reset != 0) != cudaSuccess ||
-      read_gemm_bwd_device_error(&c, reset != 0) != cudaSuccess)
+      read_gemm_bwd_device_error(&c, reset != 0) != cudaSuccess ||
+      read_peer_device_error(&d, reset != 0) != cudaSuccess)
     return FLASH_PROLOGUE_ERR_CUDA;
-  *value = a | b | c;
+  *value = a | b | c | d;
   return FLASH_PROLOGUE_OK;
 }
 
@@ -420,12 +421,13 @@ int bwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
              const int64_t dq_strides[4], void* grad_k, const int64_t dk_strides[4],
              float* grad_rmsnorm_weight, float* grad_scales, void* workspace,
              size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D, float eps,
-             int dtype, void* stream) {
+             int dtype, void* stream, const BwdReduce& red = BwdReduce{}) {
   int st = common_checks(q, q_strides, k, k_strides, rmsnorm_weight, scales, sin, sin_strides, cos,
                          cos_strides, B, H, N, D, eps, dtype);
   if (st != FLASH_PROLOGUE_OK) return st;
   if (!grad_rmsnorm_weight || !grad_scales) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (red.peers && B * H * N == 0) return FLASH_PROLOGUE_ERR_UNSUPPORTED;  // every rank must add rows
   if (B * H * N == 0) {
     // No rows: the parameter gradients are exactly zero.
     if (cudaMemsetAsync(grad_rmsnorm_weight, 0, sizeof(float) * 2 * D, s) != cudaSuccess ||
@@ -473,7 +475,7 @@ int bwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
       t.partials = static_cast<float*>(workspace);
       t.rms[0] = rms_q; t.rms[1] = rms_k;
       t.B = B; t.N = N; t.H = (int)H; t.eps = eps;
-      cudaError_t err = launch_bwd_tma(t, grad_rmsnorm_weight, grad_scales, dtype, (int)D, inv, s);
+      cudaError_t err = launch_bwd_tma(t, grad_rmsnorm_weight, grad_scales, dtype, (int)D, inv, red, s);
       return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
     }
   }
@@ -496,7 +498,7 @@ int bwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
   a.rms[0] = rms_q; a.rms[1] = rms_k;
   a.B = B; a.N = N; a.H = (int)H; a.eps = eps;
   a.g = g;
-  cudaError_t err = launch_bwd(a, grad_rmsnorm_weight, grad_scales, dtype, (int)D, vec, inv, s);
+  cudaError_t err = launch_bwd(a, grad_rmsnorm_weight, grad_scales, dtype, (int)D, vec, inv, red, s);
   return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
 }
 
@@ -517,6 +519,29 @@ int flash_prologue_bwd(const void* q, const int64_t q_strides[4], const void* k,
                   sin_strides, cos, cos_strides, grad_q_out, gq_strides, grad_k_out, gk_strides,
                   grad_q, dq_strides, grad_k, dk_strides, grad_rmsnorm_weight, grad_scales,
                   workspace, workspace_bytes, B, H, N, D, eps, dtype, stream);
+}
+
+int flash_prologue_bwd_dp(const void* q, const int64_t q_strides[4], const void* k,
+                          const int64_t k_strides[4], const float* rmsnorm_weight, const float* scales,
+                          const float* sin, const int64_t sin_strides[3], const float* cos,
+                          const int64_t cos_strides[3], const void* grad_q_out, const int64_t gq_strides[4],
+                          const void* grad_k_out, const int64_t gk_strides[4], void* grad_q,
+                          const int64_t dq_strides[4], void* grad_k, const int64_t dk_strides[4],
+                          float* grad_rmsnorm_weight, float* grad_scales, void* workspace,
+                          size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D, float eps,
+                          int dtype, const flash_prologue_peers* peers, uint32_t epoch, void* stream) {
+  if (!peers || epoch == 0) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  if (peers->world < 1 || peers->world > FLASH_PROLOGUE_MAX_PEERS || peers->rank < 0 ||
+      peers->rank >= peers->world || peers->max_cols % 32 != 0 || peers->max_cols < 2 * D + H ||
+      peers->wait_ms < 0 || peers->wait_ms > 60000)
+    return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  BwdReduce red;
+  red.peers = peers;
+  red.epoch = epoch;
+  return bwd_impl(q, q_strides, k, k_strides, nullptr, nullptr, false, rmsnorm_weight, scales, sin,
+                  sin_strides, cos, cos_strides, grad_q_out, gq_strides, grad_k_out, gk_strides,
+                  grad_q, dq_strides, grad_k, dk_strides, grad_rmsnorm_weight, grad_scales,
+                  workspace, workspace_bytes, B, H, N, D, eps, dtype, stream, red);
 }
 
 int flash_prologue_inverse_bwd(const void* q_out, const int64_t q_out_strides[4],

@@ -262,7 +262,7 @@ int64_t bwd_grid(const Geometry& g, int H, int D, int dtype, bool vec, bool inv)
 }
 
 cudaError_t launch_bwd(const BwdArgs& a, float* dw, float* ds, int dtype, int D, bool vec,
-                       bool inv, cudaStream_t stream) {
+                       bool inv, const BwdReduce& red, cudaStream_t stream) {
   const void* fn = bwd_kernel_for(dtype, D, vec, inv);
   if (!fn) return cudaErrorInvalidValue;
   const size_t smem = bwd_smem_bytes(a.H, D, inv);
@@ -274,7 +274,7 @@ cudaError_t launch_bwd(const BwdArgs& a, float* dw, float* ds, int dtype, int D,
   void* args[] = {&launch_args};
   cudaError_t err = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kThreads), args, smem, stream);
   if (err != cudaSuccess) return err;
-  return launch_bwd_finalize(a.partials, grid, 2 * D + a.H, 2 * D, dw, ds, stream);
+  return launch_bwd_reduce(a.partials, grid, 2 * D + a.H, 2 * D, dw, ds, red, stream);
 }
 
 cudaError_t launch_bwd_finalize(const float* partials, int64_t G, int C, int two_d, float* dw,

@@ -12,6 +12,8 @@
 
 #include "prologue_common.cuh"
 
+struct flash_prologue_peers;  // include/flash_prologue.h
+
 namespace flash_prologue {
 
 // Launches fn<<<grid, block, smem, stream>>>(args...) through cudaLaunchKernel
@@ -163,12 +165,14 @@ size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv = 
 cudaError_t read_device_error(int* value, bool reset);
 cudaError_t read_gemm_device_error(int* value, bool reset);
 cudaError_t read_gemm_bwd_device_error(int* value, bool reset);
+cudaError_t read_peer_device_error(int* value, bool reset);
 // One thread waits (bounded by `tries` polls) on a barrier nothing arrives at.
 cudaError_t launch_selftest_wait_timeout(uint32_t tries, cudaStream_t stream);
 int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype, bool inv = false);
 cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream);
+struct BwdReduce;
 cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype, int D,
-                           bool inv, cudaStream_t stream);
+                           bool inv, const BwdReduce& red, cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // Geometry of a problem (layout-dependent, device-independent).
@@ -182,6 +186,16 @@ int64_t persistent_grid(const void* kernel, size_t smem_bytes, int64_t n_items,
 cudaError_t launch_bwd_finalize(const float* partials, int64_t G, int C, int two_d, float* dw,
                                 float* ds, cudaStream_t stream);
 
+// Where the backward's per-CTA partials go: the local fixed-order sum (peers
+// null), or that sum added over the ranks of a peer group in one kernel
+// (peer_reduce.cu).
+struct BwdReduce {
+  const flash_prologue_peers* peers = nullptr;
+  uint32_t epoch = 0;
+};
+cudaError_t launch_bwd_reduce(const float* partials, int64_t G, int C, int two_d, float* dw, float* ds,
+                              const BwdReduce& red, cudaStream_t stream);
+
 // Launchers; return a cudaError_t from the launch.
 cudaError_t launch_fwd(const FwdArgs& a, int dtype, int D, bool vec, cudaStream_t stream);
 
@@ -190,6 +204,6 @@ cudaError_t launch_fwd(const FwdArgs& a, int dtype, int D, bool vec, cudaStream_
 int64_t bwd_grid(const Geometry& g, int H, int D, int dtype, bool vec, bool inv = false);
 size_t bwd_smem_bytes(int H, int D, bool inv = false);
 cudaError_t launch_bwd(const BwdArgs& a, float* dw, float* ds, int dtype, int D, bool vec,
-                       bool inv, cudaStream_t stream);
+                       bool inv, const BwdReduce& red, cudaStream_t stream);
 
 }  // namespace flash_prologue

@@ -633,7 +633,7 @@ cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t s
 }
 
 cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype, int D,
-                           bool inv, cudaStream_t stream) {
+                           bool inv, const BwdReduce& red, cudaStream_t stream) {
   const void* fn = tma_kernel_for(true, dtype, D, inv);
   if (!fn) return cudaErrorInvalidValue;
   const size_t smem = tma_smem_bytes(a.p, D, 4, a.H, inv);
@@ -648,7 +648,7 @@ cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype,
   void* args[] = {&launch_args};
   err = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kTmaBwdThreads), args, smem, stream);
   if (err != cudaSuccess) return err;
-  return launch_bwd_finalize(a.partials, grid, 2 * D + a.H, 2 * D, dw, ds, stream);
+  return launch_bwd_reduce(a.partials, grid, 2 * D + a.H, 2 * D, dw, ds, red, stream);
 }
 
 }  // namespace flash_prologue

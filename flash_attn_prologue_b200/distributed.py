@@ -19,6 +19,10 @@ Two modes over one packed [2*D + H] FP32 buffer:
 has produced the partials, so it overlaps whatever the main stream runs next
 (the next step's forward, or the rest of a model's backward); ``wait()`` joins
 the results back into the main stream before they are used.
+
+``PeerGroup`` replaces the library collective altogether: inside its
+``reducing()`` context the backward's own finalize kernel exchanges the
+parameter-gradient sums with the other ranks over NVLink peer memory.
 """
 from typing import Iterable, Optional
 
@@ -87,6 +91,114 @@ class ParamGradReducer:
     def wait(self):
         if self.stream is not None:
             torch.cuda.current_stream(self.stream.device).wait_stream(self.stream)
+
+
+class PeerGroup:
+    """The ranks' exchange buffers mapped into every rank, for flash_prologue_bwd_dp.
+
+    Collective to build (every rank of ``group`` calls it): each rank allocates
+    one small exchange buffer and flag array (zeros, from torch's allocator),
+    exports IPC handles for them, gathers every rank's handles over the process
+    group and maps the peers' buffers. Inside ``with group.reducing():`` the
+    backward of qknorm_rope_scale(backend="cute") on this device returns
+    d rmsnorm_weight and d scales already summed over the ranks: its finalize
+    kernel adds the per-CTA partials, exchanges the [2*D + H] sums over NVLink
+    and adds them in rank order (identical bits on every rank) -- no separate
+    collective, no NCCL. ``max_cols`` bounds 2*D + H (rounded up to 32).
+    All ranks must run the same backward calls in the same order inside the
+    context. One process per GPU on one node, at most 8 ranks (two ranks on
+    one GPU are refused: their kernels would wait on each other). A rank that
+    does not arrive within ``wait_ms`` leaves NaN gradients and the device
+    error word set on the others instead of a hang.
+    """
+
+    def __init__(self, group: Optional[dist.ProcessGroup] = None, max_cols: int = 1024,
+                 device: Optional[torch.device] = None, wait_ms: int = 2000):
+        import ctypes
+        from . import _lib
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _lib.MAX_PEERS:
+            raise ValueError(f"PeerGroup spans at most {_lib.MAX_PEERS} ranks")
+        if not 0 < wait_ms <= 60000:
+            raise ValueError("wait_ms must be in 1 .. 60000")
+        self.max_cols = -(-max_cols // 32) * 32
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        nd, nf = ctypes.c_size_t(), ctypes.c_size_t()
+        _lib.check(lib.flash_prologue_peer_buffer_bytes(self.world, self.max_cols, ctypes.byref(nd),
+                                                        ctypes.byref(nf)), "flash_prologue_peer_buffer_bytes")
+        self.data = torch.zeros(nd.value // 4, dtype=torch.float32, device=self.device)
+        self.flags = torch.zeros(nf.value // 4, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)
+        mine = [str(torch.cuda.get_device_properties(self.device).uuid)]
+        for t in (self.data, self.flags):
+            h = (ctypes.c_char * 64)()
+            off = ctypes.c_int64()
+            _lib.check(lib.flash_prologue_ipc_handle(_lib.ptr(t), h, ctypes.byref(off)), "flash_prologue_ipc_handle")
+            mine.append((bytes(h), off.value))
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=group)
+        if len({e[0] for e in every}) != self.world:
+            raise ValueError("PeerGroup needs one GPU per rank")
+        self._opened = []
+        self.desc = _lib.PeersDesc()
+        self.desc.world, self.desc.rank, self.desc.max_cols = self.world, self.rank, self.max_cols
+        self.desc.wait_ms = wait_ms
+        for r, (_, (hd, od), (hf, of)) in enumerate(every):
+            if r == self.rank:
+                pd, pf = self.data.data_ptr(), self.flags.data_ptr()
+            else:
+                pd, pf = (self._open(lib, h, o) for h, o in ((hd, od), (hf, of)))
+            self.desc.data[r], self.desc.flags[r] = pd, pf
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def _open(self, lib, handle, offset):
+        import ctypes
+        from . import _lib
+        p = ctypes.c_void_p()
+        _lib.check(lib.flash_prologue_ipc_open(handle, offset, ctypes.byref(p)), "flash_prologue_ipc_open")
+        self._opened.append((p.value, offset))
+        return p.value
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch
+
+    def reducing(self):
+        """Context in which this device's cute backward reduces over the group."""
+        import contextlib
+
+        @contextlib.contextmanager
+        def ctx():
+            prev = _ACTIVE_PEER_GROUPS.get(self.device.index)
+            _ACTIVE_PEER_GROUPS[self.device.index] = self
+            try:
+                yield self
+            finally:
+                if prev is None:
+                    _ACTIVE_PEER_GROUPS.pop(self.device.index, None)
+                else:
+                    _ACTIVE_PEER_GROUPS[self.device.index] = prev
+        return ctx()
+
+    def close(self):
+        """Unmaps the peers' buffers (after every rank's last use: call it after a barrier)."""
+        from . import _lib
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        for p, off in self._opened:
+            lib.flash_prologue_ipc_close(p, off)
+        self._opened = []
+
+
+_ACTIVE_PEER_GROUPS = {}
+
+
+def active_peer_group(device: torch.device):
+    """The PeerGroup whose reducing() context is open for ``device``, or None."""
+    return _ACTIVE_PEER_GROUPS.get(device.index) if _ACTIVE_PEER_GROUPS else None
 
 
 def allreduce_module_grads(modules: Iterable[torch.nn.Module],

@@ -25,6 +25,7 @@ backward), any ``eps > 0`` and D in {32, 64, 128, 256} with BF16/FP16/FP32 are
 accepted, and the weight/scale gradients are reduced in a fixed order (no float
 atomics). Nothing here runs on the CPU: the device work is the CUDA library.
 """
+import ctypes
 from typing import Optional, Tuple
 
 import torch
@@ -253,19 +254,28 @@ def cute_backward(q, k, rmsnorm_weight, scales, sin, cos, grad_q_out, grad_k_out
     w = rmsnorm_weight.float().contiguous()
     s = scales.float().contiguous()
     lib = _lib.load()
+    from .distributed import active_peer_group
+    peers = active_peer_group(q.device)
     with _DeviceGuard(q.device):
         nbytes = bwd_workspace_bytes(B, H, N, D, q.dtype) if q.numel() else 0
         workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
-        status = lib.flash_prologue_bwd(
-            _lib.ptr(q), _lib.strides4(q), _lib.ptr(k), _lib.strides4(k),
-            _lib.ptr(w), _lib.ptr(s),
-            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
-            _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
-            _lib.ptr(grad_q), _lib.strides4(grad_q), _lib.ptr(grad_k), _lib.strides4(grad_k),
-            _lib.ptr(grad_w), _lib.ptr(grad_s),
-            _lib.ptr(workspace), workspace.numel(),
-            B, H, N, D, float(eps), _lib.DTYPE_CODES[q.dtype], _lib.stream_of(q.device))
-    _lib.check(status, "flash_prologue_bwd")
+        args = (_lib.ptr(q), _lib.strides4(q), _lib.ptr(k), _lib.strides4(k),
+                _lib.ptr(w), _lib.ptr(s),
+                _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+                _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
+                _lib.ptr(grad_q), _lib.strides4(grad_q), _lib.ptr(grad_k), _lib.strides4(grad_k),
+                _lib.ptr(grad_w), _lib.ptr(grad_s),
+                _lib.ptr(workspace), workspace.numel(),
+                B, H, N, D, float(eps), _lib.DTYPE_CODES[q.dtype])
+        if peers is None:
+            status = lib.flash_prologue_bwd(*args, _lib.stream_of(q.device))
+            what = "flash_prologue_bwd"
+        else:
+            # d rmsnorm_weight / d scales summed over the group's ranks in the finalize kernel
+            status = lib.flash_prologue_bwd_dp(*args, ctypes.byref(peers.desc), peers.next_epoch(),
+                                               _lib.stream_of(q.device))
+            what = "flash_prologue_bwd_dp"
+    _lib.check(status, what)
     return grad_q, grad_k, grad_w, grad_s
 
 

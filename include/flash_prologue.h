@@ -331,6 +331,85 @@ FLASH_PROLOGUE_API int flash_prologue_device_error(int* value, int reset);
  */
 FLASH_PROLOGUE_API int flash_prologue_selftest_wait_timeout(uint32_t tries, void* stream);
 
+/*
+ * ---------------------------------------------------------------------------
+ * Data-parallel backward over peer memory (NVLink / NVSwitch). The reference
+ * has no distributed code; these entry points make the one collective of the
+ * data-parallel step -- the sum over ranks of d rmsnorm_weight and d scales --
+ * part of the backward's own finalize kernel instead of a separate library
+ * collective. One process per GPU, all GPUs of one node.
+ *
+ * A peer group is one small exchange buffer and one flag array per rank,
+ * allocated by each rank (from its own allocator, zero-filled) and mapped into
+ * every other rank's address space with the IPC calls below. The descriptor
+ * lists every rank's buffers as mapped in the calling process (its own at
+ * index `rank`).
+ */
+#define FLASH_PROLOGUE_MAX_PEERS 8
+
+typedef struct flash_prologue_peers {
+  int32_t world;      /* ranks in the group, 1 .. FLASH_PROLOGUE_MAX_PEERS          */
+  int32_t rank;       /* the calling rank                                         */
+  int32_t max_cols;   /* floats per exchange row: >= 2 * D + H, a multiple of 32  */
+  int32_t wait_ms;    /* bound on each wait for a peer, ms; 0 = 2000, at most 60000 */
+  float* data[FLASH_PROLOGUE_MAX_PEERS];      /* [2][world][max_cols] FP32 per rank */
+  uint32_t* flags[FLASH_PROLOGUE_MAX_PEERS];  /* [2][world][max_cols / 32] per rank */
+} flash_prologue_peers;
+
+/* Bytes of one rank's exchange buffer and flag array for a group shape. */
+FLASH_PROLOGUE_API int flash_prologue_peer_buffer_bytes(int32_t world, int32_t max_cols,
+                                                        size_t* data_bytes, size_t* flag_bytes);
+
+/*
+ * IPC mapping of device memory between the processes of one node:
+ * `handle` (64 bytes) names the allocation holding `dev_ptr`, `offset` is
+ * dev_ptr's offset in it; open maps a peer's handle and returns its pointer
+ * plus offset; close unmaps what open returned. The caller's allocation must
+ * stay alive while any peer has it open.
+ */
+FLASH_PROLOGUE_API int flash_prologue_ipc_handle(const void* dev_ptr, void* handle, int64_t* offset);
+FLASH_PROLOGUE_API int flash_prologue_ipc_open(const void* handle, int64_t offset, void** dev_ptr);
+FLASH_PROLOGUE_API int flash_prologue_ipc_close(void* dev_ptr, int64_t offset);
+
+/*
+ * flash_prologue_bwd whose d rmsnorm_weight / d scales come out summed over
+ * the ranks of `peers`: the finalize kernel adds the per-CTA partials in a
+ * fixed order, writes the rank's sum into every rank's exchange buffer over
+ * NVLink, sets its flags there, waits (bounded) for every rank's flags in its
+ * own buffer and adds the ranks' sums in rank order -- the same bits on every
+ * rank and run to run. `epoch` must be the same on every rank and grow by one
+ * per call (start at 1); calls alternate between two halves of the buffers, so
+ * a rank may run one call ahead of the slowest. Every rank must make the same
+ * calls in the same order. A wait that runs out (a rank that did not arrive)
+ * records the device error word and writes NaN gradients; nothing hangs. The
+ * ranks must be on different GPUs: two ranks on one GPU would be separate
+ * kernels waiting on each other, which the GPU need not run side by side.
+ */
+FLASH_PROLOGUE_API int flash_prologue_bwd_dp(const void* q, const int64_t q_strides[4],
+                       const void* k, const int64_t k_strides[4],
+                       const float* rmsnorm_weight, const float* scales,
+                       const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3],
+                       const void* grad_q_out, const int64_t gq_strides[4],
+                       const void* grad_k_out, const int64_t gk_strides[4],
+                       void* grad_q, const int64_t dq_strides[4],
+                       void* grad_k, const int64_t dk_strides[4],
+                       float* grad_rmsnorm_weight, float* grad_scales,
+                       void* workspace, size_t workspace_bytes,
+                       int64_t B, int64_t H, int64_t N, int64_t D,
+                       float eps, int dtype, const flash_prologue_peers* peers,
+                       uint32_t epoch, void* stream);
+
+/*
+ * Test form of the group reduction: every rank of `peers` emulated by one
+ * cooperative launch on the current GPU (all buffers local). partials[r]:
+ * rank r's [G, C] per-CTA partials; dw[r] / ds[r]: its outputs. For tests on
+ * one GPU of the protocol flash_prologue_bwd_dp runs across GPUs.
+ */
+FLASH_PROLOGUE_API int flash_prologue_peer_reduce_emulated(const float* const* partials, int64_t G,
+                       int32_t C, int32_t two_d, float* const* dw, float* const* ds,
+                       const flash_prologue_peers* peers, uint32_t epoch, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
