@@ -14,17 +14,16 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// Looked up once per process (a function-local static: thread-safe initialisation).
 inline EncodeTiledFn tensor_map_encoder() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  static const EncodeTiledFn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
+      return reinterpret_cast<EncodeTiledFn>(p);
+    return EncodeTiledFn(nullptr);
+  }();
   return fn;
 }
 
@@ -46,9 +45,24 @@ inline bool encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int r
     e[i] = 1;
   }
   for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
-  return fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  auto encode = [&] {
+    return fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = encode();
+  static thread_local bool bound = false;
+  if (r != CUDA_SUCCESS && !bound) {
+    // The driver call needs a context bound to the calling thread, and a thread
+    // whose first CUDA call this is (an autograd worker, say) has none yet: bind
+    // the current device's primary context through the runtime (once per
+    // thread) and retry, instead of failing and sending the call down the
+    // register path, which groups the parameter-gradient sums differently.
+    bound = true;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) r = encode();
+  }
+  return r == CUDA_SUCCESS;
 }
 
 }  // namespace flash_prologue
