@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
   const int lane = threadIdx.x & 31;
   Cursor4 cur;
   if (warp == kTmaConsumerWarps) {  // ---------------- producer ----------------
-    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_stream = policy_evict_normal();
     const uint64_t pol_table = policy_evict_last();
     int k = 0;
     bool failed = false;
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
   if (warp >= kTmaConsumerWarps) {  // ---------------- producer warpgroup ----------------
     setmaxnreg_dec<kTmaBwdProducerRegs>();
     if (warp != kTmaConsumerWarps) return;
-    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_stream = policy_evict_normal();
     const uint64_t pol_table = policy_evict_last();
     int k = 0;
     for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {

@@ -60,10 +60,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-// L2 eviction policies for bulk copies.
-__device__ __forceinline__ uint64_t policy_evict_first() {
+// L2 eviction policies for bulk copies. The streamed prologue tiles use the
+// normal policy: evict_first on them measured 1% (backward) to 4% (forward)
+// slower at C2 sizes.
+__device__ __forceinline__ uint64_t policy_evict_normal() {
   uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 __device__ __forceinline__ uint64_t policy_evict_last() {
