@@ -14,9 +14,12 @@ exchange buffers. GPU, on one device:
   ``reducing()`` equals the plain one, and the IPC export works;
 * a rank that never arrives: the wait gives up after the descriptor's
   wait_ms, the gradients come out NaN, the device error word is set, and the
-  context stays usable (one kernel, no second launch waited on).
+  context stays usable (one kernel, no second launch waited on);
+* one process per visible GPU (2 to 8 GPUs): every rank holds the rank-order
+  sum of the ranks' own gradients, bit for bit.
 
-CPU: argument checks that return before touching the device.
+CPU: argument checks that return before touching the device, and PeerGroup's
+own checks on a one-rank gloo group.
 """
 import ctypes
 import datetime
@@ -88,6 +91,25 @@ def test_argument_checks_without_a_device_call():
                                        null, s4, null, s4, null, null, null, 0, 1, 16, 8, 64, 1e-5, 0,
                                        ctypes.byref(desc) if desc is not None else None, epoch, None)
         assert st == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_peer_group_rejects_bad_arguments_before_any_device_work():
+    """PeerGroup's host checks run first: a one-rank gloo group on CPU reaches them."""
+    import torch.distributed as dist
+    from flash_attn_prologue_b200.distributed import PeerGroup
+    started = False
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ["MASTER_PORT"] = str(_free_port())
+        dist.init_process_group("gloo", rank=0, world_size=1, timeout=datetime.timedelta(seconds=30))
+        started = True
+    try:
+        for bad in (0, -5, 60001):
+            with pytest.raises(ValueError, match="wait_ms"):
+                PeerGroup(wait_ms=bad)
+    finally:
+        if started:
+            dist.destroy_process_group()
 
 
 def _desc_bad(rank, world, max_cols):
@@ -302,15 +324,16 @@ def _two_rank_worker(rank, world, port, steps, errq):
 
 
 @pytest.mark.gpu
-def test_peer_group_two_processes_two_gpus():
-    """Two ranks on two GPUs: the reduced gradients are the rank-order sum, bit for bit, on both."""
+def test_peer_group_processes_on_every_visible_gpu():
+    """One rank per visible GPU (2 to 8): the reduced gradients are the rank-order sum, bit for
+    bit, on every rank, four steps in a row (both buffer halves, each reused)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import time
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
-    world, port = 2, _free_port()
+    world, port = min(torch.cuda.device_count(), _lib.MAX_PEERS), _free_port()
     procs = [ctx.Process(target=_two_rank_worker, args=(r, world, port, 4, errq)) for r in range(world)]
     for p in procs:
         p.start()
