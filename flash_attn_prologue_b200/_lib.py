@@ -73,6 +73,10 @@ SIGNATURES = {
                                _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
                                _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64,
                                ctypes.c_float, ctypes.c_int, _vp, ctypes.c_uint32, _vp], ctypes.c_int),
+    "flash_prologue_inverse_bwd_dp": ([_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _vp, _vp, _i64p,
+                                       _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p,
+                                       _vp, _vp, _vp, ctypes.c_size_t, _i64, _i64, _i64, _i64,
+                                       ctypes.c_float, ctypes.c_int, _vp, ctypes.c_uint32, _vp], ctypes.c_int),
     "flash_prologue_peer_buffer_bytes": ([ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t),
                                           ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "flash_prologue_ipc_handle": ([_vp, _vp, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),

@@ -502,6 +502,20 @@ int bwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
   return err == cudaSuccess ? FLASH_PROLOGUE_OK : FLASH_PROLOGUE_ERR_CUDA;
 }
 
+// The reduction of a data-parallel backward: a valid group (its rank inside it,
+// a row long enough for 2 * D + H sums, a wait bound within limits) and an epoch
+// of at least 1.
+bool peer_reduce_of(const flash_prologue_peers* peers, uint32_t epoch, int64_t D, int64_t H, BwdReduce* red) {
+  if (!peers || epoch == 0) return false;
+  if (peers->world < 1 || peers->world > FLASH_PROLOGUE_MAX_PEERS || peers->rank < 0 ||
+      peers->rank >= peers->world || peers->max_cols % 32 != 0 || peers->max_cols < 2 * D + H ||
+      peers->wait_ms < 0 || peers->wait_ms > 60000)
+    return false;
+  red->peers = peers;
+  red->epoch = epoch;
+  return true;
+}
+
 }  // namespace
 
 extern "C" {
@@ -530,18 +544,33 @@ int flash_prologue_bwd_dp(const void* q, const int64_t q_strides[4], const void*
                           float* grad_rmsnorm_weight, float* grad_scales, void* workspace,
                           size_t workspace_bytes, int64_t B, int64_t H, int64_t N, int64_t D, float eps,
                           int dtype, const flash_prologue_peers* peers, uint32_t epoch, void* stream) {
-  if (!peers || epoch == 0) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
-  if (peers->world < 1 || peers->world > FLASH_PROLOGUE_MAX_PEERS || peers->rank < 0 ||
-      peers->rank >= peers->world || peers->max_cols % 32 != 0 || peers->max_cols < 2 * D + H ||
-      peers->wait_ms < 0 || peers->wait_ms > 60000)
-    return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   BwdReduce red;
-  red.peers = peers;
-  red.epoch = epoch;
+  if (!peer_reduce_of(peers, epoch, D, H, &red)) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   return bwd_impl(q, q_strides, k, k_strides, nullptr, nullptr, false, rmsnorm_weight, scales, sin,
                   sin_strides, cos, cos_strides, grad_q_out, gq_strides, grad_k_out, gk_strides,
                   grad_q, dq_strides, grad_k, dk_strides, grad_rmsnorm_weight, grad_scales,
                   workspace, workspace_bytes, B, H, N, D, eps, dtype, stream, red);
+}
+
+int flash_prologue_inverse_bwd_dp(const void* q_out, const int64_t q_out_strides[4],
+                                  const void* k_out, const int64_t k_out_strides[4],
+                                  const float* rms_q, const float* rms_k,
+                                  const float* rmsnorm_weight, const float* scales, const float* sin,
+                                  const int64_t sin_strides[3], const float* cos,
+                                  const int64_t cos_strides[3], const void* grad_q_out,
+                                  const int64_t gq_strides[4], const void* grad_k_out,
+                                  const int64_t gk_strides[4], void* grad_q,
+                                  const int64_t dq_strides[4], void* grad_k,
+                                  const int64_t dk_strides[4], float* grad_rmsnorm_weight,
+                                  float* grad_scales, void* workspace, size_t workspace_bytes,
+                                  int64_t B, int64_t H, int64_t N, int64_t D, float eps, int dtype,
+                                  const flash_prologue_peers* peers, uint32_t epoch, void* stream) {
+  BwdReduce red;
+  if (!peer_reduce_of(peers, epoch, D, H, &red)) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  return bwd_impl(q_out, q_out_strides, k_out, k_out_strides, rms_q, rms_k, true, rmsnorm_weight,
+                  scales, sin, sin_strides, cos, cos_strides, grad_q_out, gq_strides, grad_k_out,
+                  gk_strides, grad_q, dq_strides, grad_k, dk_strides, grad_rmsnorm_weight,
+                  grad_scales, workspace, workspace_bytes, B, H, N, D, eps, dtype, stream, red);
 }
 
 int flash_prologue_inverse_bwd(const void* q_out, const int64_t q_out_strides[4],

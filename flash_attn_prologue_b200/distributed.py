@@ -99,9 +99,10 @@ class PeerGroup:
     Collective to build (every rank of ``group`` calls it): each rank allocates
     one small exchange buffer and flag array (zeros, from torch's allocator),
     exports IPC handles for them, gathers every rank's handles over the process
-    group and maps the peers' buffers. Inside ``with group.reducing():`` the
-    backward of qknorm_rope_scale(backend="cute") on this device returns
-    d rmsnorm_weight and d scales already summed over the ranks: its finalize
+    group and maps the peers' buffers. Inside ``with group.reducing():`` every
+    prologue backward on this device (qknorm_rope_scale(backend="cute"), its
+    inverse form, qknorm_rope_scale_qkv and the fused QKV projection's backward)
+    returns d rmsnorm_weight and d scales already summed over the ranks: its finalize
     kernel adds the per-CTA partials, exchanges the [2*D + H] sums over NVLink
     and adds them in rank order (identical bits on every rank) -- no separate
     collective, no NCCL. ``max_cols`` bounds 2*D + H (rounded up to 32).

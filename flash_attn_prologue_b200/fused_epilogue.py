@@ -253,30 +253,36 @@ def cute_backward(q, k, rmsnorm_weight, scales, sin, cos, grad_q_out, grad_k_out
     cos4, cos_str = _table(cos, B, N, D // 2)
     w = rmsnorm_weight.float().contiguous()
     s = scales.float().contiguous()
-    lib = _lib.load()
-    from .distributed import active_peer_group
-    peers = active_peer_group(q.device)
     with _DeviceGuard(q.device):
         nbytes = bwd_workspace_bytes(B, H, N, D, q.dtype) if q.numel() else 0
         workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
-        args = (_lib.ptr(q), _lib.strides4(q), _lib.ptr(k), _lib.strides4(k),
-                _lib.ptr(w), _lib.ptr(s),
-                _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
-                _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
-                _lib.ptr(grad_q), _lib.strides4(grad_q), _lib.ptr(grad_k), _lib.strides4(grad_k),
-                _lib.ptr(grad_w), _lib.ptr(grad_s),
-                _lib.ptr(workspace), workspace.numel(),
-                B, H, N, D, float(eps), _lib.DTYPE_CODES[q.dtype])
-        if peers is None:
-            status = lib.flash_prologue_bwd(*args, _lib.stream_of(q.device))
-            what = "flash_prologue_bwd"
-        else:
-            # d rmsnorm_weight / d scales summed over the group's ranks in the finalize kernel
-            status = lib.flash_prologue_bwd_dp(*args, ctypes.byref(peers.desc), peers.next_epoch(),
-                                               _lib.stream_of(q.device))
-            what = "flash_prologue_bwd_dp"
-    _lib.check(status, what)
+        _call_bwd("flash_prologue_bwd", q.device,
+                  _lib.ptr(q), _lib.strides4(q), _lib.ptr(k), _lib.strides4(k),
+                  _lib.ptr(w), _lib.ptr(s),
+                  _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+                  _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
+                  _lib.ptr(grad_q), _lib.strides4(grad_q), _lib.ptr(grad_k), _lib.strides4(grad_k),
+                  _lib.ptr(grad_w), _lib.ptr(grad_s),
+                  _lib.ptr(workspace), workspace.numel(),
+                  B, H, N, D, float(eps), _lib.DTYPE_CODES[q.dtype])
     return grad_q, grad_k, grad_w, grad_s
+
+
+def _call_bwd(name, device, *args):
+    """Calls a backward entry point (flash_prologue_bwd / flash_prologue_inverse_bwd) on the
+    device's current stream. Inside an open ``PeerGroup.reducing()`` context for the device it
+    calls the entry's ``_dp`` form instead, whose finalize kernel returns d rmsnorm_weight and
+    d scales already summed over the group's ranks."""
+    from .distributed import active_peer_group
+    lib = _lib.load()
+    peers = active_peer_group(device)
+    if peers is None:
+        status = getattr(lib, name)(*args, _lib.stream_of(device))
+    else:
+        name = name + "_dp"
+        status = getattr(lib, name)(*args, ctypes.byref(peers.desc), peers.next_epoch(),
+                                    _lib.stream_of(device))
+    _lib.check(status, name)
 
 
 @qknorm_rope_scale_cute_backward_op.register_fake
@@ -412,20 +418,18 @@ def qknorm_rope_scale_cute_inverse_backward_op(
     cos4, cos_str = _table(cos, B, N, D // 2)
     w = rmsnorm_weight.float().contiguous()
     s = scales.float().contiguous()
-    lib = _lib.load()
     with _DeviceGuard(q_out.device):
         nbytes = bwd_workspace_bytes(B, H, N, D, q_out.dtype) if q_out.numel() else 0
         workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q_out.device)
-        status = lib.flash_prologue_inverse_bwd(
-            _lib.ptr(q_out), _lib.strides4(q_out), _lib.ptr(k_out), _lib.strides4(k_out),
-            _lib.ptr(rq), _lib.ptr(rk), _lib.ptr(w), _lib.ptr(s),
-            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
-            _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
-            _lib.ptr(grad_q), _lib.strides4(grad_q), _lib.ptr(grad_k), _lib.strides4(grad_k),
-            _lib.ptr(grad_w), _lib.ptr(grad_s),
-            _lib.ptr(workspace), workspace.numel(),
-            B, H, N, D, float(eps), _lib.DTYPE_CODES[q_out.dtype], _lib.stream_of(q_out.device))
-    _lib.check(status, "flash_prologue_inverse_bwd")
+        _call_bwd("flash_prologue_inverse_bwd", q_out.device,
+                  _lib.ptr(q_out), _lib.strides4(q_out), _lib.ptr(k_out), _lib.strides4(k_out),
+                  _lib.ptr(rq), _lib.ptr(rk), _lib.ptr(w), _lib.ptr(s),
+                  _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+                  _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
+                  _lib.ptr(grad_q), _lib.strides4(grad_q), _lib.ptr(grad_k), _lib.strides4(grad_k),
+                  _lib.ptr(grad_w), _lib.ptr(grad_s),
+                  _lib.ptr(workspace), workspace.numel(),
+                  B, H, N, D, float(eps), _lib.DTYPE_CODES[q_out.dtype])
     return grad_q, grad_k, grad_w, grad_s
 
 
@@ -483,20 +487,18 @@ def backward_into(q4, k4, rmsnorm_weight, scales, sin, cos, grad_q_out, grad_k_o
     cos4, cos_str = _table(cos, B, N, D // 2)
     w = rmsnorm_weight.float().contiguous()
     s = scales.float().contiguous()
-    lib = _lib.load()
     with _DeviceGuard(q4.device):
         nbytes = bwd_workspace_bytes(B, H, N, D, q4.dtype) if q4.numel() else 0
         workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q4.device)
-        status = lib.flash_prologue_bwd(
-            _lib.ptr(q4), _lib.strides4(q4), _lib.ptr(k4), _lib.strides4(k4),
-            _lib.ptr(w), _lib.ptr(s),
-            _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
-            _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
-            _lib.ptr(dq4), _lib.strides4(dq4), _lib.ptr(dk4), _lib.strides4(dk4),
-            _lib.ptr(grad_w), _lib.ptr(grad_s),
-            _lib.ptr(workspace), workspace.numel(),
-            B, H, N, D, float(eps), _lib.DTYPE_CODES[q4.dtype], _lib.stream_of(q4.device))
-    _lib.check(status, "flash_prologue_bwd")
+        _call_bwd("flash_prologue_bwd", q4.device,
+                  _lib.ptr(q4), _lib.strides4(q4), _lib.ptr(k4), _lib.strides4(k4),
+                  _lib.ptr(w), _lib.ptr(s),
+                  _lib.ptr(sin4), _lib.strides3(sin_str), _lib.ptr(cos4), _lib.strides3(cos_str),
+                  _lib.ptr(gq), _lib.strides4(gq), _lib.ptr(gk), _lib.strides4(gk),
+                  _lib.ptr(dq4), _lib.strides4(dq4), _lib.ptr(dk4), _lib.strides4(dk4),
+                  _lib.ptr(grad_w), _lib.ptr(grad_s),
+                  _lib.ptr(workspace), workspace.numel(),
+                  B, H, N, D, float(eps), _lib.DTYPE_CODES[q4.dtype])
     return grad_w, grad_s
 
 

@@ -401,6 +401,27 @@ FLASH_PROLOGUE_API int flash_prologue_bwd_dp(const void* q, const int64_t q_stri
                        uint32_t epoch, void* stream);
 
 /*
+ * flash_prologue_inverse_bwd with the same group reduction of d rmsnorm_weight
+ * and d scales (same epoch sequence as flash_prologue_bwd_dp: one counter per
+ * group, whichever of the two a call uses).
+ */
+FLASH_PROLOGUE_API int flash_prologue_inverse_bwd_dp(const void* q_out, const int64_t q_out_strides[4],
+                       const void* k_out, const int64_t k_out_strides[4],
+                       const float* rms_q, const float* rms_k,
+                       const float* rmsnorm_weight, const float* scales,
+                       const float* sin, const int64_t sin_strides[3],
+                       const float* cos, const int64_t cos_strides[3],
+                       const void* grad_q_out, const int64_t gq_strides[4],
+                       const void* grad_k_out, const int64_t gk_strides[4],
+                       void* grad_q, const int64_t dq_strides[4],
+                       void* grad_k, const int64_t dk_strides[4],
+                       float* grad_rmsnorm_weight, float* grad_scales,
+                       void* workspace, size_t workspace_bytes,
+                       int64_t B, int64_t H, int64_t N, int64_t D,
+                       float eps, int dtype, const flash_prologue_peers* peers,
+                       uint32_t epoch, void* stream);
+
+/*
  * Test form of the group reduction: every rank of `peers` emulated by one
  * cooperative launch on the current GPU (all buffers local). partials[r]:
  * rank r's [G, C] per-CTA partials; dw[r] / ds[r]: its outputs. For tests on

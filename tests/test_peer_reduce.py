@@ -10,8 +10,9 @@ exchange buffers. GPU, on one device:
   result bit-identical to the fixed-order sum restated in numpy (warp-strided
   partial rows, warps in order, ranks in order);
 * flash_prologue_bwd_dp with a one-rank group gives flash_prologue_bwd's bits;
-* PeerGroup in a one-rank NCCL process group: the autograd backward inside
-  ``reducing()`` equals the plain one, and the IPC export works;
+* PeerGroup in a one-rank NCCL process group: inside ``reducing()`` each
+  backward path (regular, inverse, packed QKV gradient) goes through its _dp
+  entry and equals the plain call bit for bit; the IPC export works;
 * a rank that never arrives: the wait gives up after the descriptor's
   wait_ms, the gradients come out NaN, the device error word is set, and the
   context stays usable (one kernel, no second launch waited on);
@@ -202,10 +203,43 @@ def _free_port():
         return sk.getsockname()[1]
 
 
+def _backward_paths(q4, k4, w, s, sin, cos, gq, gk):
+    """Each prologue backward reachable from the public API: name -> f(use_group) -> grads."""
+    from flash_attn_prologue_b200 import qknorm_rope_scale, qknorm_rope_scale_qkv
+    q, k = q4[0].permute(1, 0, 2), k4[0].permute(1, 0, 2)
+    g_q, g_k = gq[0].permute(1, 0, 2), gk[0].permute(1, 0, 2)
+
+    def regular(ctx):
+        args = [t.detach().clone().requires_grad_(i < 4) for i, t in enumerate((q, k, w, s, sin, cos))]
+        out = qknorm_rope_scale(*args, backend="cute")
+        with ctx():
+            return torch.autograd.grad(out, args[:4], (g_q, g_k))
+
+    def inverse(ctx):
+        qq, kk = q4.detach().clone().requires_grad_(), k4.detach().clone().requires_grad_()
+        ww, ss = w.detach().clone().requires_grad_(), s.detach().clone().requires_grad_()
+        s4, c4 = (t[:, None].permute(1, 0, 2)[None] for t in (sin, cos))
+        qo, ko, _, _ = torch.ops.flash_prologue.qknorm_rope_scale_cute_inverse(qq, kk, ww, ss, s4, c4, 1e-5)
+        with ctx():
+            return torch.autograd.grad((qo, ko), (qq, kk, ww, ss), (gq, gk))
+
+    def packed(ctx):
+        qkv = torch.stack((q, k, q), dim=1).detach().requires_grad_()
+        ww, ss = w.detach().clone().requires_grad_(), s.detach().clone().requires_grad_()
+        qo, ko, _ = qknorm_rope_scale_qkv(qkv, ww, ss, sin, cos)
+        with ctx():
+            return torch.autograd.grad((qo, ko), (qkv, ww, ss), (g_q, g_k))
+
+    return {"regular": regular, "inverse": inverse, "packed": packed}
+
+
 @pytest.mark.gpu
-def test_peer_group_context_in_a_one_rank_process_group():
+def test_every_backward_path_dispatches_to_the_group_in_a_one_rank_process_group():
+    """Inside reducing(), every backward path calls its _dp entry (the group's epoch
+    advances once per call) and a one-rank group returns the plain call's bits."""
+    import contextlib
     import torch.distributed as dist
-    from flash_attn_prologue_b200 import prepare_backend, qknorm_rope_scale
+    from flash_attn_prologue_b200 import prepare_backend
     from flash_attn_prologue_b200.distributed import PeerGroup
     prepare_backend("cute")
     started = False
@@ -216,24 +250,16 @@ def test_peer_group_context_in_a_one_rank_process_group():
                                 device_id=torch.device("cuda", 0))
         started = True
     try:
-        q4, k4, w, s, sin, cos, gq, gk = _c2_problem(seed=3)
-        q, k = q4[0].permute(1, 0, 2), k4[0].permute(1, 0, 2)
-        g_q, g_k = gq[0].permute(1, 0, 2), gk[0].permute(1, 0, 2)
         pg = PeerGroup(device=torch.device("cuda", 0), max_cols=2 * 64 + 16)
-        results = []
-        for use in (False, True):
-            args = [t.detach().clone().requires_grad_(i < 4) for i, t in enumerate((q, k, w, s, sin, cos))]
-            out = qknorm_rope_scale(*args, backend="cute")
-            if use:
-                with pg.reducing():
-                    grads = torch.autograd.grad(out, args[:4], (g_q, g_k))
-            else:
-                grads = torch.autograd.grad(out, args[:4], (g_q, g_k))
-            results.append(grads)
-        torch.cuda.synchronize()
-        for a, b in zip(*results):
-            assert torch.equal(_bits(a), _bits(b))
-        assert pg.epoch == 1
+        paths = _backward_paths(*_c2_problem(seed=3))
+        for n, (name, fn) in enumerate(paths.items(), start=1):
+            plain = fn(contextlib.nullcontext)
+            reduced = fn(pg.reducing)
+            torch.cuda.synchronize()
+            assert pg.epoch == n, name
+            for a, b in zip(plain, reduced):
+                assert torch.equal(_bits(a), _bits(b)), name
+        assert _lib.device_error(reset=True) == 0
         pg.close()
     finally:
         if started:
