@@ -126,7 +126,9 @@ def load():
 
 
 def set_path(mode: int) -> None:
-    """0: TMA pipeline when the layout allows (default); 1: register path only."""
+    """0: automatic (default): TMA pipeline when the layout allows, outputs by TMA
+    stores where measured faster; 1: register path only; 2: TMA pipeline, outputs
+    always by TMA stores; 3: TMA pipeline, outputs by the lanes' stores."""
     check(load().flash_prologue_set_path(int(mode)), "flash_prologue_set_path")
 
 

@@ -194,7 +194,10 @@ int common_checks(const void* q, const int64_t* qs, const void* k, const int64_t
   return st;
 }
 
-// 0: automatic (TMA pipeline when the layout allows it), 1: register path only.
+// 0: automatic (TMA pipeline when the layout allows it, outputs stored as
+// use_tma_stores picks), 1: register path only, 2: TMA pipeline with TMA-stored
+// outputs wherever the output views allow, 3: TMA pipeline with the consumer
+// lanes' stores.
 int g_path_mode = 0;
 
 constexpr int kFwdStages = kTmaFwdStages;
@@ -225,6 +228,20 @@ bool tma_tensor_ok(const void* p, const int64_t s[4], int64_t B, int64_t D, int 
                                    : dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   return encode_tensor_map(&out->map, type, 5, p, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// How the TMA kernels' outputs leave: written by the consumer lanes with 16-byte
+// stores, or written back over the stage's input tiles and stored by the
+// producer warp with one TMA tensor store per tile. Measured on B200 (paired,
+// interleaved runs, identical bits): TMA stores take 0.956-0.978 of the lane
+// stores' time in the D = 64 backward at every packed layout tested (0.992
+// dense), and 0.95 in the D = 64 forward once each CTA streams about 900 tiles
+// (neutral at 200-450, 1.04 slower at 110); at D = 128 they are 1.04-1.05
+// (backward) and 1.12-1.15 (forward) slower. `grid` is the forward's grid.
+bool use_tma_stores(bool bwd, int64_t D, const TmaPlan& p, int64_t grid) {
+  if (g_path_mode == 2) return true;
+  if (g_path_mode != 0 || D != 64) return false;
+  return bwd || (grid > 0 && p.n_tiles >= 512 * grid);
 }
 
 // sin/cos tables the TMA path can read (bulk copies): rows of D/2 contiguous floats.
@@ -258,7 +275,7 @@ FLASH_PROLOGUE_API int flash_prologue_selftest_wait_timeout(uint32_t tries, void
 }
 
 FLASH_PROLOGUE_API int flash_prologue_set_path(int mode) {
-  if (mode != 0 && mode != 1) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
+  if (mode < 0 || mode > 3) return FLASH_PROLOGUE_ERR_INVALID_ARGUMENT;
   g_path_mode = mode;
   return FLASH_PROLOGUE_OK;
 }
@@ -311,7 +328,7 @@ int fwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
                    table_vec_ok(sin, sin_strides) && table_vec_ok(cos, cos_strides);
   const bool heads_inner = heads_inner_layout(q_strides, H, N);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (g_path_mode == 0 && vec) {
+  if (g_path_mode != 1 && vec) {
     TmaFwdArgs t{};
     t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kFwdStages);
     if (tma_tensor_ok(q, q_strides, B, D, dtype, heads_inner, t.p, &t.in[0]) &&
@@ -319,6 +336,13 @@ int fwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
         tma_table_ok(sin, sin_strides, N, D) && tma_table_ok(cos, cos_strides, N, D)) {
       t.out[0] = q_out; t.out[1] = k_out;
       t.so[0] = rows(q_out_strides); t.so[1] = rows(k_out_strides);
+      t.store_tma = !rms_q &&
+                    use_tma_stores(false, D, t.p,
+                                   g_path_mode == 0 && D == 64
+                                       ? tma_grid(false, t.p, (int)H, (int)D, dtype, false)
+                                       : 0) &&
+                    tma_tensor_ok(q_out, q_out_strides, B, D, dtype, heads_inner, t.p, &t.out_map[0]) &&
+                    tma_tensor_ok(k_out, k_out_strides, B, D, dtype, heads_inner, t.p, &t.out_map[1]);
       t.w = rmsnorm_weight; t.scales = scales; t.sin = sin; t.cos = cos;
       t.sin_b = sin_strides[0]; t.cos_b = cos_strides[0];
       t.rms[0] = rms_q; t.rms[1] = rms_k;
@@ -455,7 +479,7 @@ int bwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
                    view_vec_ok(grad_q, dq_strides, es) && view_vec_ok(grad_k, dk_strides, es) &&
                    table_vec_ok(sin, sin_strides) && table_vec_ok(cos, cos_strides);
   const bool heads_inner = heads_inner_layout(q_strides, H, N);
-  if (g_path_mode == 0 && vec) {
+  if (g_path_mode != 1 && vec) {
     TmaBwdArgs t{};
     t.p = plan_tma(B, H, N, (int)D, dtype, heads_inner, kBwdStages);
     if (tma_tensor_ok(q, q_strides, B, D, dtype, heads_inner, t.p, &t.in[0]) &&
@@ -470,6 +494,9 @@ int bwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
         return FLASH_PROLOGUE_ERR_WORKSPACE;
       t.dx[0] = grad_q; t.dx[1] = grad_k;
       t.sd[0] = rows(dq_strides); t.sd[1] = rows(dk_strides);
+      t.store_tma = !inv && use_tma_stores(true, D, t.p, 0) &&
+                    tma_tensor_ok(grad_q, dq_strides, B, D, dtype, heads_inner, t.p, &t.out[0]) &&
+                    tma_tensor_ok(grad_k, dk_strides, B, D, dtype, heads_inner, t.p, &t.out[1]);
       t.w = rmsnorm_weight; t.scales = scales; t.sin = sin; t.cos = cos;
       t.sin_b = sin_strides[0]; t.cos_b = cos_strides[0];
       t.partials = static_cast<float*>(workspace);

@@ -127,6 +127,8 @@ struct alignas(64) TmaTensor {
 
 struct TmaFwdArgs {
   TmaTensor in[2];      // q, k
+  TmaTensor out_map[2]; // q_out, k_out as TMA store targets (when store_tma)
+  int store_tma;        // 1: outputs staged in the stage's q / k tiles and stored by TMA
   void* out[2];         // q_out, k_out
   RowStrides so[2];
   const float* w;
@@ -143,6 +145,8 @@ struct TmaFwdArgs {
 
 struct TmaBwdArgs {
   TmaTensor in[4];      // q, grad_q_out, k, grad_k_out
+  TmaTensor out[2];     // dq, dk as TMA store targets (when store_tma)
+  int store_tma;        // 1: dq / dk staged in the stage's q / k tiles and stored by TMA
   void* dx[2];          // dq, dk
   RowStrides sd[2];
   const float* w;

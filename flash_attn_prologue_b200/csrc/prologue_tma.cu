@@ -102,6 +102,29 @@ __device__ __forceinline__ void lds_f8(float (&v)[kChunk], const unsigned char* 
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+// 8 values of the activation dtype to shared memory (16 or 32 bytes).
+template <typename T>
+__device__ __forceinline__ void sts_chunk(unsigned char* p, const Chunk<T>& c) {
+  uint4* p4 = reinterpret_cast<uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < Chunk<T>::kWords / 4; ++i)
+    p4[i] = make_uint4(c.w[4 * i + 0], c.w[4 * i + 1], c.w[4 * i + 2], c.w[4 * i + 3]);
+}
+
+// Output tiles of one stage, which the consumers wrote over the stage's
+// input tiles in the same half-major layout: lane t < 2 issues one tiled TMA
+// store of tensor t's tile (rows outside the tensor are not written) and waits
+// until the store has read shared memory, so the stage can be refilled.
+__device__ __forceinline__ void store_stage_out(const TmaTensor* out, const unsigned char* st,
+                                                int in_stride_tiles, const TileCoords& tc, int lane) {
+  if (lane < 2) {
+    tma_store_5d(&out[lane].map, st + lane * in_stride_tiles * kTmaTileBytes, 0, tc.i0, tc.o0, 0, tc.b);
+    bulk_commit_group();
+    bulk_wait_group_read0();
+  }
+  __syncwarp();
+}
+
 }  // namespace
 
 // Forward that saves r: one tile's r values, staged by the consumers in the
@@ -132,9 +155,12 @@ __device__ __forceinline__ void store_tile_r(const TmaFwdArgs& a, const TileCoor
 
 // ---------------------------------------------------------------------------
 // Forward. RMS = true also stores each row's r to a.rms (inverse formulation).
-template <typename T, int D, bool RMS>
+// TS = true writes q_out / k_out back into the stage's q / k tiles and lets the
+// producer warp store them with TMA.
+template <typename T, int D, bool RMS, bool TS>
 __global__ void __launch_bounds__(kTmaThreads, 2)
     prologue_fwd_tma_kernel(const __grid_constant__ TmaFwdArgs a) {
+  static_assert(!(RMS && TS), "one lagging producer task per variant");
   using S_ = TmaShape<T, D>;
   constexpr int HALF = S_::HALF;
   constexpr int L = S_::L;
@@ -177,6 +203,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
         store_tile_r<S_::ROWS>(a, tile_coords(a.p, lag), reinterpret_cast<const float*>(st + r_off), lane);
         lag.advance(a.p.radix);
       }
+      if (TS && k >= S) {  // the consumers have written tile k - S's outputs into this stage
+        store_stage_out(a.out_map, st, 1, tile_coords(a.p, lag), lane);
+        lag.advance(a.p.radix);
+      }
       const TileCoords tc = tile_coords(a.p, cur);
       const int64_t n_first = a.p.heads_inner ? (int64_t)tc.o0 : (int64_t)tc.i0;
       const int np = a.p.heads_inner ? tc.vo : tc.vi;
@@ -193,6 +223,17 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
                                reinterpret_cast<const float*>(smem + s * stage_bytes + r_off), lane);
         lag.advance(a.p.radix);
       }
+    }
+    if constexpr (TS) {
+      if (!failed) {  // outputs of the last (up to S) tiles, once the consumers are done
+        for (int j = k > S ? k - S : 0; j < k; ++j) {
+          const int s = j % S;
+          if (!mbar_wait(&empty[s], (j / S) & 1)) break;
+          store_stage_out(a.out_map, smem + s * stage_bytes, 1, tile_coords(a.p, lag), lane);
+          lag.advance(a.p.radix);
+        }
+      }
+      if (lane < 2) bulk_wait_group0();
     }
     return;
   }
@@ -240,10 +281,18 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       if (RMS && c == 0) reinterpret_cast<float*>(const_cast<unsigned char*>(st) + r_off)[t * S_::ROWS + r] = rr;
       Chunk<T> out1, out2;
       fwd_lane(x1, x2, rr, wa, wb, sn, cs, t == 0, t == 0 ? e_s[h] : 1.f, out1, out2);
-      T* yp = ytile + (int64_t)i_l * so_inner + (int64_t)o_l * so_outer;
-      store_stream<T, true>(yp, out1);
-      store_stream<T, true>(yp + HALF, out2);
+      if constexpr (TS) {
+        // Over this lane's own chunks of the q / k tile, read above.
+        unsigned char* xw = const_cast<unsigned char*>(row);
+        sts_chunk(xw, out1);
+        sts_chunk(xw + S_::HALF_TILE, out2);
+      } else {
+        T* yp = ytile + (int64_t)i_l * so_inner + (int64_t)o_l * so_outer;
+        store_stream<T, true>(yp, out1);
+        store_stream<T, true>(yp + HALF, out2);
+      }
     }
+    if constexpr (TS) fence_proxy_async_smem();  // the producer's TMA stores read these tiles
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
@@ -262,9 +311,12 @@ __device__ __forceinline__ float load_saved_r(const TmaBwdArgs& a, const TileCoo
   return __ldg(a.rms[t] + ((int64_t)tc.b * a.H + h) * a.N + n);
 }
 
-template <typename T, int D, bool INV>
+// TS = true writes dq / dk back into the stage's q / k tiles and lets the
+// producer warp store them with TMA (regular backward only).
+template <typename T, int D, bool INV, bool TS>
 __global__ void __launch_bounds__(kTmaBwdThreads, 2)
     prologue_bwd_tma_kernel(const __grid_constant__ TmaBwdArgs a) {
+  static_assert(!(INV && TS), "the inverse backward reads its outputs' tiles as inputs");
   using S_ = TmaShape<T, D>;
   constexpr int HALF = S_::HALF;
   constexpr int L = S_::L;
@@ -312,17 +364,37 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
     const uint64_t pol_stream = policy_evict_normal();
     const uint64_t pol_table = policy_evict_last();
     int k = 0;
+    bool failed = false;
+    Cursor4 lag;  // TS: the tile whose outputs go out next, S tiles behind
+    if constexpr (TS) lag.init(blockIdx.x, a.p.radix);
     for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {
       const int s = k % S;
-      if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) break;
+      if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) { failed = true; break; }
       const TileCoords tc = tile_coords(a.p, cur);
       unsigned char* st = smem + s * stage_bytes;
+      if constexpr (TS) {
+        if (k >= S) {  // the consumers have written tile k - S's outputs into this stage
+          store_stage_out(a.out, st, 2, tile_coords(a.p, lag), lane);
+          lag.advance(a.p.radix);
+        }
+      }
       const int64_t n_first = a.p.heads_inner ? (int64_t)tc.o0 : (int64_t)tc.i0;
       const int np = a.p.heads_inner ? tc.vo : tc.vi;
       if (lane == 0) mbar_arrive_expect_tx(&full[s], 4 * kTmaTileBytes + 2 * np * HALF * 4);
       __syncwarp();
       issue_stage<D>(a.in, 4, a.sin, a.cos, a.sin_b, a.cos_b, n_first, np, tc, st, table_bytes,
                      &full[s], lane, pol_stream, pol_table);
+    }
+    if constexpr (TS) {
+      if (!failed) {  // outputs of the last (up to S) tiles, once the consumers are done
+        for (int j = k > S ? k - S : 0; j < k; ++j) {
+          const int s = j % S;
+          if (!mbar_wait(&empty[s], (j / S) & 1)) break;
+          store_stage_out(a.out, smem + s * stage_bytes, 2, tile_coords(a.p, lag), lane);
+          lag.advance(a.p.radix);
+        }
+      }
+      if (lane < 2) bulk_wait_group0();
     }
     return;
   }
@@ -439,10 +511,18 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       else
         lane_dx<T>(n1, n2, dnw1, dnw2, re, __fdividef(__fmul_rn(rr, dsum * (1.0f / (float)D)), e), out1,
                    out2);
-      T* dp = dtile + (int64_t)i_l * sd_inner + (int64_t)o_l * sd_outer;
-      store_stream<T, true>(dp, out1);
-      store_stream<T, true>(dp + HALF, out2);
+      if constexpr (TS) {
+        // Over this lane's own chunks of the q / k tile, read above.
+        unsigned char* xw = const_cast<unsigned char*>(tile_x) + r * S_::HALF_BYTES + j0 * sizeof(T);
+        sts_chunk(xw, out1);
+        sts_chunk(xw + S_::HALF_TILE, out2);
+      } else {
+        T* dp = dtile + (int64_t)i_l * sd_inner + (int64_t)o_l * sd_outer;
+        store_stream<T, true>(dp, out1);
+        store_stream<T, true>(dp + HALF, out2);
+      }
     }
+    if constexpr (TS) fence_proxy_async_smem();  // the producer's TMA stores read these tiles
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
@@ -537,25 +617,28 @@ size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv) {
 }
 
 template <typename T, int D>
-static const void* fwd_tma_ptr(bool rms) {
-  return rms ? reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, true>)
-             : reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, false>);
+static const void* fwd_tma_ptr(bool rms, bool ts) {
+  return rms  ? reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, true, false>)
+         : ts ? reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, false, true>)
+              : reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, false, false>);
 }
 template <typename T, int D>
-static const void* bwd_tma_ptr(bool inv) {
-  return inv ? reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, true>)
-             : reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, false>);
+static const void* bwd_tma_ptr(bool inv, bool ts) {
+  return inv  ? reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, true, false>)
+         : ts ? reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, false, true>)
+              : reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, false, false>);
 }
 
 // `inv`: the inverse backward, or for the forward the variant that stores r.
-static const void* tma_kernel_for(bool bwd, int dtype, int D, bool inv) {
-#define FP_TMA_CASE(T)                                                       \
-  switch (D) {                                                               \
-    case 32: return bwd ? bwd_tma_ptr<T, 32>(inv) : fwd_tma_ptr<T, 32>(inv);     \
-    case 64: return bwd ? bwd_tma_ptr<T, 64>(inv) : fwd_tma_ptr<T, 64>(inv);     \
-    case 128: return bwd ? bwd_tma_ptr<T, 128>(inv) : fwd_tma_ptr<T, 128>(inv);  \
-    case 256: return bwd ? bwd_tma_ptr<T, 256>(inv) : fwd_tma_ptr<T, 256>(inv);  \
-    default: return nullptr;                                                 \
+// `ts`: the variant whose outputs leave through TMA stores.
+static const void* tma_kernel_for(bool bwd, int dtype, int D, bool inv, bool ts = false) {
+#define FP_TMA_CASE(T)                                                                       \
+  switch (D) {                                                                               \
+    case 32: return bwd ? bwd_tma_ptr<T, 32>(inv, ts) : fwd_tma_ptr<T, 32>(inv, ts);         \
+    case 64: return bwd ? bwd_tma_ptr<T, 64>(inv, ts) : fwd_tma_ptr<T, 64>(inv, ts);         \
+    case 128: return bwd ? bwd_tma_ptr<T, 128>(inv, ts) : fwd_tma_ptr<T, 128>(inv, ts);      \
+    case 256: return bwd ? bwd_tma_ptr<T, 256>(inv, ts) : fwd_tma_ptr<T, 256>(inv, ts);      \
+    default: return nullptr;                                                                 \
   }
   switch (dtype) {
     case 0: FP_TMA_CASE(__nv_bfloat16)
@@ -619,7 +702,7 @@ int64_t tma_grid(bool bwd, const TmaPlan& p, int H, int D, int dtype, bool inv) 
 }
 
 cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t stream) {
-  const void* fn = tma_kernel_for(false, dtype, D, a.rms[0] != nullptr);
+  const void* fn = tma_kernel_for(false, dtype, D, a.rms[0] != nullptr, a.store_tma != 0);
   if (!fn) return cudaErrorInvalidValue;
   const size_t smem = tma_smem_bytes(a.p, D, 2, a.H, a.rms[0] != nullptr);
   cudaError_t err = prepare_kernel(fn, smem);
@@ -634,7 +717,7 @@ cudaError_t launch_fwd_tma(const TmaFwdArgs& a, int dtype, int D, cudaStream_t s
 
 cudaError_t launch_bwd_tma(const TmaBwdArgs& a, float* dw, float* ds, int dtype, int D,
                            bool inv, const BwdReduce& red, cudaStream_t stream) {
-  const void* fn = tma_kernel_for(true, dtype, D, inv);
+  const void* fn = tma_kernel_for(true, dtype, D, inv, a.store_tma != 0);
   if (!fn) return cudaErrorInvalidValue;
   const size_t smem = tma_smem_bytes(a.p, D, 4, a.H, inv);
   cudaError_t err = prepare_kernel(fn, smem);

@@ -100,6 +100,39 @@ __device__ __forceinline__ void tma_load_5d_hint(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// Tiled TMA store of a 5-D box from shared memory (bulk-group completion), the
+// inverse of tma_load_5d_hint: c0 is 0 or a 16-byte multiple, no coordinate is
+// negative, and rows outside the tensor are not written.
+__device__ __forceinline__ void tma_store_5d(const CUtensorMap* map, const void* src, int32_t c0,
+                                             int32_t c1, int32_t c2, int32_t c3, int32_t c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4, %5}], [%6];"
+      ::"l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+        "r"(smem_u32(src))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until the committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until at most N of the most recently committed bulk-store groups are
+// still reading shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until the committed bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Makes this thread's generic-proxy shared-memory writes visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Warpgroup register reallocation: all 128 threads of a warpgroup execute the
 // same instruction. An increase waits until the block's pool (registers per
 // thread at launch x threads) has room, so the split must fit that pool.

@@ -170,28 +170,6 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t c0,
       ::"l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(src))
       : "memory");
 }
-__device__ __forceinline__ void bulk_commit_group() {
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-// Waits until the committed bulk stores have finished reading shared memory.
-__device__ __forceinline__ void bulk_wait_group_read0() {
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-// Waits until at most N of the most recently committed bulk-store groups are
-// still reading shared memory.
-template <int N>
-__device__ __forceinline__ void bulk_wait_group_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-// Waits until the committed bulk stores have completed.
-__device__ __forceinline__ void bulk_wait_group0() {
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
-// Makes this thread's generic-proxy shared-memory writes visible to the async (TMA) proxy.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -307,8 +307,13 @@ FLASH_PROLOGUE_API int flash_prologue_bwd_noalloc(const void* q, const int64_t q
  * mode 0 (default): the TMA pipelined kernels whenever the views
  * allow them (16-byte aligned, rows contiguous along the inner row dim, positive
  * 16-byte-multiple outer strides, sin/cos rows contiguous, a tensor map the
- * driver accepts), else the register-path kernels; mode 1: register path
- * only. Both paths compute bit-identical results.
+ * driver accepts), else the register-path kernels, with the outputs of the
+ * pipelined forward and regular backward leaving through TMA tensor stores
+ * where that measured faster (D = 64; the forward only for long runs per CTA)
+ * and through the lanes' 16-byte stores otherwise; mode 1: register path
+ * only; mode 2: pipelined kernels with TMA-stored outputs wherever the output
+ * views allow; mode 3: pipelined kernels with lane stores. Every mode computes
+ * bit-identical results.
  * No counterpart in the reference (which has a single kernel per op).
  */
 FLASH_PROLOGUE_API int flash_prologue_set_path(int mode);

@@ -276,15 +276,20 @@ def test_backward_bit_reproducible():
 
 
 # ----------------------------------------------------------------------------
-# The two kernel paths (TMA pipeline and register path) compute the same
-# per-row arithmetic: outputs and dq/dk must be bit-identical; the parameter
-# gradients differ only in the (fixed) grouping of their partial sums.
+# The kernel paths (TMA pipeline with TMA-stored or lane-stored outputs, and the
+# register path) compute the same per-row arithmetic: outputs and dq/dk must be
+# bit-identical; the parameter gradients of the register path differ only in
+# the (fixed) grouping of their partial sums, and the two TMA store forms share
+# the grid, so theirs are bit-identical too.
+
+PATH_MODES = (0, 1, 2, 3)  # automatic, register path, TMA stores forced, lane stores forced
+
 
 def _run_both_paths(args, gq, gk):
     from flash_attn_prologue_b200 import _lib
     results = []
     try:
-        for mode in (0, 1):
+        for mode in PATH_MODES:
             _lib.set_path(mode)
             a = [t.detach().requires_grad_(i < 4) for i, t in enumerate(args)]
             out = qknorm_rope_scale(*a, backend="cute")
@@ -316,10 +321,15 @@ def test_bulk_copy_and_register_paths_agree(layout, d):
     s = 0.2 * torch.randn(h, 1, 1, generator=g, device="cuda")
     gq = torch.randn(q.shape, generator=g, device="cuda").to(torch.bfloat16)
     gk = torch.randn(k.shape, generator=g, device="cuda").to(torch.bfloat16)
-    (o0, g0), (o1, g1) = _run_both_paths((q, k, w, s, ang.sin(), ang.cos()), gq, gk)
-    assert torch.equal(o0[0], o1[0]) and torch.equal(o0[1], o1[1])
-    assert torch.equal(g0[0], g1[0]) and torch.equal(g0[1], g1[1])
-    assert rel_err(g0[2], g1[2]) < 1e-5 and rel_err(g0[3], g1[3]) < 1e-5
+    res = _run_both_paths((q, k, w, s, ang.sin(), ang.cos()), gq, gk)
+    o0, g0 = res[0]
+    for mode, (o1, g1) in zip(PATH_MODES[1:], res[1:]):
+        assert torch.equal(o0[0], o1[0]) and torch.equal(o0[1], o1[1]), mode
+        assert torch.equal(g0[0], g1[0]) and torch.equal(g0[1], g1[1]), mode
+        if mode == 1:
+            assert rel_err(g0[2], g1[2]) < 1e-5 and rel_err(g0[3], g1[3]) < 1e-5
+        else:
+            assert torch.equal(g0[2], g1[2]) and torch.equal(g0[3], g1[3]), mode
 
 
 @pytest.mark.parametrize("d", [64, 128])
