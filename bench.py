@@ -49,7 +49,7 @@ BWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 6 + HEAD_DIM * 4
 # scaled to a launch by the tokens it processes. Writes still dirty in L2 when a
 # kernel ends are not counted by the capture, so traffic reads slightly below
 # the algorithmic bytes.
-NCU_TRAFFIC_BYTES_PER_TOKEN = {"fwd": 8163, "bwd": 12388}
+NCU_TRAFFIC_BYTES_PER_TOKEN = {"fwd": 8179, "bwd": 12367}
 # sm__pipe_tensor_cycles_active (% of active cycles) of the fused QKV GEMM +
 # prologue kernel in one ncu capture at C5's full size (summary kept under
 # profiles/qkv_gemm_pair_c5_t65536.md).
@@ -863,6 +863,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the C1/inverse/QKV-step/C5 timings reported beside the headline")
+    ap.add_argument("--store", choices=["auto", "tma", "lane"], default="auto",
+                    help="how the pipelined prologue kernels store their outputs: the library's "
+                         "measured choice (default), always TMA tensor stores, or the lanes' "
+                         "16-byte stores (for profiling one form at a size where auto picks the other)")
     ap.add_argument("--detail", default="", help="also write the JSON line, indented, to this file")
     ap.add_argument("--c5-profile-tokens", type=int, default=0,
                     help="only run the fused QKV GEMM + prologue (C5 shapes, this many tokens) three "
@@ -886,6 +890,9 @@ def main():
         run_reference(args, world, rank)
         return
     world, rank, local = dist_setup(args)
+    if args.store != "auto":
+        from flash_attn_prologue_b200 import _lib
+        _lib.set_path({"tma": 2, "lane": 3}[args.store])
     try:
         run_ours(args, world, rank, local)
     finally:
