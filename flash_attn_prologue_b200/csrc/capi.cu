@@ -237,11 +237,14 @@ bool tma_tensor_ok(const void* p, const int64_t s[4], int64_t B, int64_t D, int 
 // stores' time in the D = 64 backward at every packed layout tested (0.992
 // dense), and 0.95 in the D = 64 forward once each CTA streams about 900 tiles
 // (neutral at 200-450, 1.04 slower at 110); at D = 128 they are 1.04-1.05
-// (backward) and 1.12-1.15 (forward) slower. `grid` is the forward's grid.
-bool use_tma_stores(bool bwd, int64_t D, const TmaPlan& p, int64_t grid) {
+// (backward) and 1.12-1.15 (forward) slower. The inverse backward gains like
+// the regular one (0.974-0.981 at D = 64); the forward that also saves r
+// (`rms`) loses everywhere (1.13-1.19), its producer already writing the r
+// values before it can refill a stage. `grid` is the forward's grid.
+bool use_tma_stores(bool bwd, bool rms, int64_t D, const TmaPlan& p, int64_t grid) {
   if (g_path_mode == 2) return true;
   if (g_path_mode != 0 || D != 64) return false;
-  return bwd || (grid > 0 && p.n_tiles >= 512 * grid);
+  return bwd || (!rms && grid > 0 && p.n_tiles >= 512 * grid);
 }
 
 // sin/cos tables the TMA path can read (bulk copies): rows of D/2 contiguous floats.
@@ -336,9 +339,8 @@ int fwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
         tma_table_ok(sin, sin_strides, N, D) && tma_table_ok(cos, cos_strides, N, D)) {
       t.out[0] = q_out; t.out[1] = k_out;
       t.so[0] = rows(q_out_strides); t.so[1] = rows(k_out_strides);
-      t.store_tma = !rms_q &&
-                    use_tma_stores(false, D, t.p,
-                                   g_path_mode == 0 && D == 64
+      t.store_tma = use_tma_stores(false, rms_q != nullptr, D, t.p,
+                                   g_path_mode == 0 && D == 64 && !rms_q
                                        ? tma_grid(false, t.p, (int)H, (int)D, dtype, false)
                                        : 0) &&
                     tma_tensor_ok(q_out, q_out_strides, B, D, dtype, heads_inner, t.p, &t.out_map[0]) &&
@@ -494,7 +496,7 @@ int bwd_impl(const void* q, const int64_t q_strides[4], const void* k, const int
         return FLASH_PROLOGUE_ERR_WORKSPACE;
       t.dx[0] = grad_q; t.dx[1] = grad_k;
       t.sd[0] = rows(dq_strides); t.sd[1] = rows(dk_strides);
-      t.store_tma = !inv && use_tma_stores(true, D, t.p, 0) &&
+      t.store_tma = use_tma_stores(true, false, D, t.p, 0) &&
                     tma_tensor_ok(grad_q, dq_strides, B, D, dtype, heads_inner, t.p, &t.out[0]) &&
                     tma_tensor_ok(grad_k, dk_strides, B, D, dtype, heads_inner, t.p, &t.out[1]);
       t.w = rmsnorm_weight; t.scales = scales; t.sin = sin; t.cos = cos;

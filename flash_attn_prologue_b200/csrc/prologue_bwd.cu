@@ -34,12 +34,14 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_kernel(const BwdArgs a)
   constexpr int HALF = D / 2;
   constexpr int LOG2_L = (L == 2) ? 1 : (L == 4) ? 2 : (L == 8) ? 3 : 4;
   extern __shared__ float smem[];
-  float* w_s = smem;                       // [2 * D]
-  float* e_s = w_s + 2 * D;                // [H]
-  float* ds_s = e_s + a.H;                 // [kWarps][H]
-  float* dw_s = ds_s + kWarps * a.H;       // [kWarps][D]
-  float* iw_s = dw_s + kWarps * D;         // INV: [2 * D] 1 / w
-  float* ie_s = iw_s + 2 * D;              // INV: [H] 1 / exp(scales)
+  // w and 1 / w are read as float pairs (8-byte loads), so they come first,
+  // at even offsets; the H-sized arrays, whose length may be odd, follow.
+  float* w_s = smem;                          // [2 * D]
+  float* iw_s = w_s + 2 * D;                  // INV: [2 * D] 1 / w
+  float* e_s = iw_s + (INV ? 2 * D : 0);      // [H]
+  float* ds_s = e_s + a.H;                    // [kWarps][H]
+  float* dw_s = ds_s + kWarps * a.H;          // [kWarps][D]
+  float* ie_s = dw_s + kWarps * D;            // INV: [H] 1 / exp(scales)
   for (int i = threadIdx.x; i < 2 * D; i += kThreads) w_s[i] = a.w[i];
   for (int i = threadIdx.x; i < a.H; i += kThreads) e_s[i] = (float)exp((double)a.scales[i]);
   for (int i = threadIdx.x; i < kWarps * a.H; i += kThreads) ds_s[i] = 0.f;

@@ -160,7 +160,6 @@ __device__ __forceinline__ void store_tile_r(const TmaFwdArgs& a, const TileCoor
 template <typename T, int D, bool RMS, bool TS>
 __global__ void __launch_bounds__(kTmaThreads, 2)
     prologue_fwd_tma_kernel(const __grid_constant__ TmaFwdArgs a) {
-  static_assert(!(RMS && TS), "one lagging producer task per variant");
   using S_ = TmaShape<T, D>;
   constexpr int HALF = S_::HALF;
   constexpr int L = S_::L;
@@ -193,18 +192,16 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     const uint64_t pol_table = policy_evict_last();
     int k = 0;
     bool failed = false;
-    Cursor4 lag;  // RMS: the tile whose r values go out next, S tiles behind
+    Cursor4 lag;  // RMS / TS: the tile whose r values / outputs go out next, S tiles behind
     lag.init(blockIdx.x, a.p.radix);
     for (cur.init(blockIdx.x, a.p.radix); cur.d[3] == 0; cur.advance(a.p.radix), ++k) {
       const int s = k % S;
       if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) { failed = true; break; }
       unsigned char* st = smem + s * stage_bytes;
-      if (RMS && k >= S) {  // the consumers are done with tile k - S
-        store_tile_r<S_::ROWS>(a, tile_coords(a.p, lag), reinterpret_cast<const float*>(st + r_off), lane);
-        lag.advance(a.p.radix);
-      }
-      if (TS && k >= S) {  // the consumers have written tile k - S's outputs into this stage
-        store_stage_out(a.out_map, st, 1, tile_coords(a.p, lag), lane);
+      if ((RMS || TS) && k >= S) {  // the consumers are done with tile k - S
+        const TileCoords lc = tile_coords(a.p, lag);
+        if constexpr (RMS) store_tile_r<S_::ROWS>(a, lc, reinterpret_cast<const float*>(st + r_off), lane);
+        if constexpr (TS) store_stage_out(a.out_map, st, 1, lc, lane);  // its outputs are in this stage
         lag.advance(a.p.radix);
       }
       const TileCoords tc = tile_coords(a.p, cur);
@@ -215,24 +212,18 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
       issue_stage<D>(a.in, 2, a.sin, a.cos, a.sin_b, a.cos_b, n_first, np, tc, st, table_bytes,
                      &full[s], lane, pol_stream, pol_table);
     }
-    if (RMS && !failed) {  // r of the last (up to S) tiles, once their stages are released
+    if ((RMS || TS) && !failed) {  // r / outputs of the last (up to S) tiles, once the consumers are done
       for (int j = k > S ? k - S : 0; j < k; ++j) {
         const int s = j % S;
         if (!mbar_wait(&empty[s], (j / S) & 1)) break;
-        store_tile_r<S_::ROWS>(a, tile_coords(a.p, lag),
-                               reinterpret_cast<const float*>(smem + s * stage_bytes + r_off), lane);
+        const TileCoords lc = tile_coords(a.p, lag);
+        const unsigned char* st = smem + s * stage_bytes;
+        if constexpr (RMS) store_tile_r<S_::ROWS>(a, lc, reinterpret_cast<const float*>(st + r_off), lane);
+        if constexpr (TS) store_stage_out(a.out_map, st, 1, lc, lane);
         lag.advance(a.p.radix);
       }
     }
     if constexpr (TS) {
-      if (!failed) {  // outputs of the last (up to S) tiles, once the consumers are done
-        for (int j = k > S ? k - S : 0; j < k; ++j) {
-          const int s = j % S;
-          if (!mbar_wait(&empty[s], (j / S) & 1)) break;
-          store_stage_out(a.out_map, smem + s * stage_bytes, 1, tile_coords(a.p, lag), lane);
-          lag.advance(a.p.radix);
-        }
-      }
       if (lane < 2) bulk_wait_group0();
     }
     return;
@@ -311,12 +302,12 @@ __device__ __forceinline__ float load_saved_r(const TmaBwdArgs& a, const TileCoo
   return __ldg(a.rms[t] + ((int64_t)tc.b * a.H + h) * a.N + n);
 }
 
-// TS = true writes dq / dk back into the stage's q / k tiles and lets the
-// producer warp store them with TMA (regular backward only).
+// TS = true writes dq / dk back into the stage's q / k tiles (for the inverse
+// backward: its q_out / k_out tiles) and lets the producer warp store them with
+// TMA. Each lane overwrites only the chunks it has already read.
 template <typename T, int D, bool INV, bool TS>
 __global__ void __launch_bounds__(kTmaBwdThreads, 2)
     prologue_bwd_tma_kernel(const __grid_constant__ TmaBwdArgs a) {
-  static_assert(!(INV && TS), "the inverse backward reads its outputs' tiles as inputs");
   using S_ = TmaShape<T, D>;
   constexpr int HALF = S_::HALF;
   constexpr int L = S_::L;
@@ -330,12 +321,14 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
   const int stage_bytes = tma_stage_bytes(4, table_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
   uint64_t* empty = full + S;
+  // w and 1 / w are read as float pairs (8-byte loads), so they come first,
+  // at even offsets; the H-sized arrays, whose length may be odd, follow.
   float* w_s = reinterpret_cast<float*>(empty + S);   // [2 * D]
-  float* e_s = w_s + 2 * D;                            // [H]
+  float* iw_s = w_s + 2 * D;                           // INV: [2 * D] 1 / w
+  float* e_s = iw_s + (INV ? 2 * D : 0);               // [H]
   float* ds_s = e_s + a.H;                             // [4][H]  (Q warps)
   float* dw_s = ds_s + 4 * a.H;                        // [8][D]
-  float* iw_s = dw_s + 8 * D;                          // INV: [2 * D] 1 / w
-  float* ie_s = iw_s + 2 * D;                          // INV: [H] 1 / exp(scales)
+  float* ie_s = dw_s + 8 * D;                          // INV: [H] 1 / exp(scales)
   __shared__ int wait_failed;  // a consumer warp gave up on a barrier wait
 
   if (threadIdx.x == 0) {
@@ -618,15 +611,19 @@ size_t tma_smem_bytes(const TmaPlan& p, int D, int n_tensors, int H, bool inv) {
 
 template <typename T, int D>
 static const void* fwd_tma_ptr(bool rms, bool ts) {
-  return rms  ? reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, true, false>)
-         : ts ? reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, false, true>)
-              : reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, false, false>);
+  if (rms)
+    return ts ? reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, true, true>)
+              : reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, true, false>);
+  return ts ? reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, false, true>)
+            : reinterpret_cast<const void*>(&prologue_fwd_tma_kernel<T, D, false, false>);
 }
 template <typename T, int D>
 static const void* bwd_tma_ptr(bool inv, bool ts) {
-  return inv  ? reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, true, false>)
-         : ts ? reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, false, true>)
-              : reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, false, false>);
+  if (inv)
+    return ts ? reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, true, true>)
+              : reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, true, false>);
+  return ts ? reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, false, true>)
+            : reinterpret_cast<const void*>(&prologue_bwd_tma_kernel<T, D, false, false>);
 }
 
 // `inv`: the inverse backward, or for the forward the variant that stores r.

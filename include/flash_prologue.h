@@ -308,9 +308,10 @@ FLASH_PROLOGUE_API int flash_prologue_bwd_noalloc(const void* q, const int64_t q
  * allow them (16-byte aligned, rows contiguous along the inner row dim, positive
  * 16-byte-multiple outer strides, sin/cos rows contiguous, a tensor map the
  * driver accepts), else the register-path kernels, with the outputs of the
- * pipelined forward and regular backward leaving through TMA tensor stores
- * where that measured faster (D = 64; the forward only for long runs per CTA)
- * and through the lanes' 16-byte stores otherwise; mode 1: register path
+ * pipelined kernels leaving through TMA tensor stores where that measured
+ * faster (D = 64 backward, regular or inverse; the D = 64 forward that does
+ * not save r, for long runs per CTA) and through the lanes' 16-byte stores
+ * otherwise; mode 1: register path
  * only; mode 2: pipelined kernels with TMA-stored outputs wherever the output
  * views allow; mode 3: pipelined kernels with lane stores. Every mode computes
  * bit-identical results.
