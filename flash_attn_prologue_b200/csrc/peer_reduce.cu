@@ -82,9 +82,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_finalize_kernel(const __gri
   const uint32_t half = a.epoch & 1u;
 
   // 1. this rank's fixed-order sum of its CTA partials
-  float v = 0.f;
-  if (col < a.C)
-    for (int64_t g = warp; g < a.G; g += kPeerWarps) v = __fadd_rn(v, a.partials[slot][g * a.C + col]);
+  const float v = col < a.C ? strided_column_sum(a.partials[slot], a.G, a.C, col, warp, kPeerWarps) : 0.f;
   part[warp][lane] = v;
   __syncthreads();
   if (warp == 0) {

@@ -207,9 +207,7 @@ __global__ void __launch_bounds__(kThreads) prologue_bwd_finalize_kernel(
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
-  float v = 0.f;
-  if (col < C)
-    for (int64_t g = warp; g < G; g += kWarps) v = __fadd_rn(v, partials[g * C + col]);
+  const float v = col < C ? strided_column_sum(partials, G, C, col, warp, kWarps) : 0.f;
   part[warp][lane] = v;
   __syncthreads();
   if (warp == 0 && col < C) {

@@ -469,4 +469,23 @@ __device__ __forceinline__ void thread_slots(const Geometry& g, int tid, int& c,
 }
 
 
+// Fixed-order sum of column `col` of a [G, C] FP32 array over the rows first,
+// first + step, ... (< G): ((0 + p[r0]) + p[r1]) + ... The loads of eight rows
+// are issued before their additions, so their latencies overlap, while the
+// additions keep the order (and the bits) of the one-row-at-a-time loop.
+__device__ __forceinline__ float strided_column_sum(const float* __restrict__ p, int64_t G, int C,
+                                                    int col, int first, int step) {
+  float v = 0.f;
+  int64_t g = first;
+  for (; g + 7 * (int64_t)step < G; g += 8 * (int64_t)step) {
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] = p[(g + (int64_t)u * step) * C + col];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v = __fadd_rn(v, x[u]);
+  }
+  for (; g < G; g += step) v = __fadd_rn(v, p[g * C + col]);
+  return v;
+}
+
 }  // namespace flash_prologue
