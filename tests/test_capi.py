@@ -69,6 +69,22 @@ def test_fwd_argument_checks(kwargs, status):
     assert _fwd(**kwargs) == status
 
 
+def test_path_modes_accepted_and_rejected():
+    """Modes 0-3 (automatic, register path, TMA-stored outputs, lane-stored
+    outputs) are accepted; anything else is an invalid argument and leaves the
+    current mode unchanged."""
+    lib = _lib.load()
+    try:
+        for mode in (1, 2, 3, 0):
+            assert lib.flash_prologue_set_path(mode) == 0
+        for mode in (-1, 4, 99):
+            assert lib.flash_prologue_set_path(mode) == 1  # FLASH_PROLOGUE_ERR_INVALID_ARGUMENT
+        with pytest.raises(Exception):
+            _lib.set_path(4)
+    finally:
+        lib.flash_prologue_set_path(0)
+
+
 def test_bwd_workspace_size_argument_checks():
     lib = _lib.load()
     n = ctypes.c_size_t(123)
