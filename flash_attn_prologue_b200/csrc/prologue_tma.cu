@@ -365,18 +365,30 @@ __global__ void __launch_bounds__(kTmaBwdThreads, 2)
       if (!mbar_wait(&empty[s], ((k / S) & 1) ^ 1)) { failed = true; break; }
       const TileCoords tc = tile_coords(a.p, cur);
       unsigned char* st = smem + s * stage_bytes;
-      if constexpr (TS) {
-        if (k >= S) {  // the consumers have written tile k - S's outputs into this stage
-          store_stage_out(a.out, st, 2, tile_coords(a.p, lag), lane);
-          lag.advance(a.p.radix);
-        }
-      }
       const int64_t n_first = a.p.heads_inner ? (int64_t)tc.o0 : (int64_t)tc.i0;
       const int np = a.p.heads_inner ? tc.vo : tc.vi;
       if (lane == 0) mbar_arrive_expect_tx(&full[s], 4 * kTmaTileBytes + 2 * np * HALF * 4);
       __syncwarp();
-      issue_stage<D>(a.in, 4, a.sin, a.cos, a.sin_b, a.cos_b, n_first, np, tc, st, table_bytes,
-                     &full[s], lane, pol_stream, pol_table);
+      if constexpr (TS) {
+        // The stage's gradient tiles and tables are free as soon as the
+        // consumers are done: load them first (lanes 1, 3: gradient tiles;
+        // 4, 5: tables), then store tile k - S's outputs from the q / k tiles,
+        // and load the q / k tiles (lanes 0, 2) once the stores have read them.
+        const bool early = (lane & 1) != 0 || lane >= 4;
+        if (early)
+          issue_stage<D>(a.in, 4, a.sin, a.cos, a.sin_b, a.cos_b, n_first, np, tc, st, table_bytes,
+                         &full[s], lane, pol_stream, pol_table);
+        if (k >= S) {
+          store_stage_out(a.out, st, 2, tile_coords(a.p, lag), lane);
+          lag.advance(a.p.radix);
+        }
+        if (!early)
+          issue_stage<D>(a.in, 4, a.sin, a.cos, a.sin_b, a.cos_b, n_first, np, tc, st, table_bytes,
+                         &full[s], lane, pol_stream, pol_table);
+      } else {
+        issue_stage<D>(a.in, 4, a.sin, a.cos, a.sin_b, a.cos_b, n_first, np, tc, st, table_bytes,
+                       &full[s], lane, pol_stream, pol_table);
+      }
     }
     if constexpr (TS) {
       if (!failed) {  // outputs of the last (up to S) tiles, once the consumers are done
