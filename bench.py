@@ -49,7 +49,7 @@ BWD_BYTES_PER_TOKEN = HEADS * HEAD_DIM * 2 * 6 + HEAD_DIM * 4
 # scaled to a launch by the tokens it processes. Writes still dirty in L2 when a
 # kernel ends are not counted by the capture, so traffic reads slightly below
 # the algorithmic bytes.
-NCU_TRAFFIC_BYTES_PER_TOKEN = {"fwd": 8179, "bwd": 12367}
+NCU_TRAFFIC_BYTES_PER_TOKEN = {"fwd": 8181, "bwd": 12370}
 # sm__pipe_tensor_cycles_active (% of active cycles) of the fused QKV GEMM +
 # prologue kernel in one ncu capture at C5's full size (summary kept under
 # profiles/qkv_gemm_pair_c5_t65536.md).
